@@ -1,0 +1,87 @@
+"""batch_topk_b200 -- batched fp16 top-k for NVIDIA B200 (sm_100a).
+
+Host-side mirror of fire-emblem/batch_topk's operator interface
+(include/batch_topk.cuh:10-21): the same entry-point names, argument meaning and error
+contract (cudaError_t codes, cudaErrorInvalidValue == 1 for bad arguments), called through
+the C ABI of ``lib/libbatch_topk_b200.so``.  Pointers are device addresses (ints), the
+stream is a cudaStream_t handle (int, 0 = default stream).
+
+``batch_topk_b200.torch_api`` adds tensor-level helpers (``topk``, ``topk_segmented``).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+from . import _lib
+
+CUDA_SUCCESS = 0
+CUDA_ERROR_INVALID_VALUE = 1
+MAX_K = 1024
+MAX_SEG_LEN = 1 << 26
+
+STATUS_FLAGS = {
+    1: "bulk-copy wait timed out",
+    2: "CSR offsets decreasing or beyond max_total_len",
+    4: "segment longer than the supported maximum",
+    8: "candidate certification failed",
+}
+
+
+class BatchTopkError(RuntimeError):
+    def __init__(self, code: int, what: str = ""):
+        self.code = code
+        msg = _lib.load().bt_error_string(code).decode()
+        super().__init__(f"{what}: error {code}: {msg}" if what else f"error {code}: {msg}")
+
+
+def batch_topk_half(d_input: int, seg_num: int, seg_len: int, k: int, d_output_values: int,
+                    d_output_indices: int, d_workspace: int, workspace_bytes: int,
+                    stream: int = 0) -> int:
+    """radix_topk::batch_topk_half: returns a cudaError_t code; asynchronous on `stream`."""
+    return _lib.load().bt_topk_half(d_input, seg_num, seg_len, k, d_output_values,
+                                    d_output_indices, d_workspace, workspace_bytes, stream)
+
+
+def batch_topk_half_workspace_size(seg_num: int, seg_len: int, k: int) -> int:
+    """radix_topk::batch_topk_half_workspace_size: 0 for an unsupported shape."""
+    return int(_lib.load().bt_topk_half_workspace_size(seg_num, seg_len, k))
+
+
+def batch_topk_half_segmented(d_input: int, d_offsets: int, seg_num: int, max_total_len: int,
+                              k: int, d_output_values: int, d_output_indices: int,
+                              d_workspace: int, workspace_bytes: int, stream: int = 0) -> int:
+    """CSR variant (no reference counterpart): int32 offsets[seg_num+1] on the device."""
+    return _lib.load().bt_topk_half_segmented(d_input, d_offsets, seg_num, max_total_len, k,
+                                              d_output_values, d_output_indices, d_workspace,
+                                              workspace_bytes, stream)
+
+
+def batch_topk_half_segmented_workspace_size(seg_num: int, max_total_len: int, k: int) -> int:
+    return int(_lib.load().bt_topk_half_segmented_workspace_size(seg_num, max_total_len, k))
+
+
+def workspace_status(d_workspace: int, seg_num: int = 0, stream: int = 0):
+    """Synchronously reads the device status of the last call on this workspace.
+
+    Returns (flags, stats) where stats = (exact-select chunks, reused-threshold chunks,
+    group-max selects, merged segments); stats are only counted with BT_STATS=1."""
+    stats = (C.c_uint * 4)()
+    rc = _lib.load().bt_workspace_status(d_workspace, seg_num, stream, C.byref(stats))
+    if rc < 0:
+        raise BatchTopkError(-rc, "bt_workspace_status")
+    return rc, tuple(int(v) for v in stats)
+
+
+def set_profile_events(ev_start: int | None, ev_stop: int | None) -> None:
+    """Record cudaEvent_t handles around the streaming kernel of later calls (None: off)."""
+    _lib.load().bt_set_profile_events(ev_start or None, ev_stop or None)
+
+
+def version() -> int:
+    return int(_lib.load().bt_version())
+
+
+def library_path() -> str:
+    from .build import LIB
+
+    return LIB

@@ -1,0 +1,255 @@
+// batch_topk.cu -- C ABI, argument validation, workspace layout and launch sequence.
+//
+// The public contract is the reference's radix_topk::batch_topk_half /
+// batch_topk_half_workspace_size (include/batch_topk.cuh:10-21, src/batch_topk.cu:13-60 of
+// fire-emblem/batch_topk): caller-owned buffers, cudaErrorInvalidValue on bad arguments,
+// asynchronous on the caller's stream, no host synchronisation, no allocation.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdlib>
+#include <mutex>
+
+#include "../../include/batch_topk_b200.h"
+#include "bt_kernels.cuh"
+
+namespace bt {
+namespace {
+
+constexpr int kVersion = 100;  // 0.1.0
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int groups_for_k(int k) { return k <= 64 ? 1 : (k <= 128 ? 2 : (k <= 256 ? 4 : 8)); }
+int cap_for_k(int k) { return k * 4 < 256 ? 256 : k * 4; }
+
+// Chunk slots one fixed-length segment may need: its 16-byte vectors span at most
+// ceil(len/8) + 1 when the row start is not 16-byte aligned.
+long long slots_per_segment(long long seg_len) {
+  const long long nv = (seg_len + 7) / 8 + 1;
+  return (nv + kVecPerChunk - 1) / kVecPerChunk;
+}
+
+// Upper bound on chunk slots for a CSR batch of seg_num segments totalling total_len values.
+long long csr_slot_bound(long long seg_num, long long total_len) {
+  return (total_len / 8 + 2 * seg_num) / kVecPerChunk + seg_num + 1;
+}
+
+struct Layout {
+  size_t status, thresh, chunk_start, counts, cand, total;
+};
+
+// status | seg_thresh | chunk_start (CSR) | chunk_count | candidates, 256-byte aligned.
+Layout make_layout(long long seg_num, long long slots, int cap, bool csr) {
+  Layout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+  };
+  L.status = take(16 * sizeof(uint32_t));
+  L.thresh = take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
+  L.chunk_start = csr ? take(static_cast<size_t>(seg_num + 1) * sizeof(uint32_t)) : 0;
+  L.counts = take(static_cast<size_t>(slots) * sizeof(uint32_t));
+  L.cand = take(static_cast<size_t>(slots) * cap * sizeof(uint32_t));
+  L.total = off;
+  return L;
+}
+
+bool fixed_shape_ok(int seg_num, int seg_len, int k) {
+  return seg_num > 0 && seg_len > 0 && k > 0 && k <= kMaxK && k <= seg_len &&
+         static_cast<long long>(seg_len) <= BT_MAX_SEG_LEN;
+}
+
+bool csr_shape_ok(int seg_num, long long max_total_len, int k) {
+  return seg_num > 0 && k > 0 && k <= kMaxK && max_total_len >= 0 &&
+         max_total_len < (1ll << 31);
+}
+
+struct DeviceInfo {
+  bool ready = false;
+  int sms = 0;
+  int chunk_blocks_per_sm = 0;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[64];
+cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
+int g_stats = -1;
+
+cudaError_t device_info(DeviceInfo* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    e = cudaFuncSetAttribute(chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kChunkSmemBytes));
+    if (e != cudaSuccess) return e;
+    e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.chunk_blocks_per_sm, chunk_kernel,
+                                                      kThreads, kChunkSmemBytes);
+    if (e != cudaSuccess) return e;
+    if (d.chunk_blocks_per_sm < 1) return cudaErrorInvalidConfiguration;
+    if (g_stats < 0) {
+      const char* s = std::getenv("BT_STATS");
+      g_stats = (s && s[0] == '1') ? 1 : 0;
+    }
+    d.ready = true;
+  }
+  *out = d;
+  return cudaSuccess;
+}
+
+cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaStream_t stream) {
+  DeviceInfo di;
+  cudaError_t e = device_info(&di);
+  if (e != cudaSuccess) return e;
+  p.stats = g_stats > 0 ? 1 : 0;
+  p.reuse = 1;
+  if (csr) {
+    csr_prep_kernel<<<1, 1024, 0, stream>>>(p);
+  } else {
+    const int blocks = static_cast<int>((p.seg_num + 255) / 256);
+    init_kernel<<<blocks, 256, 0, stream>>>(p);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const long long resident = static_cast<long long>(di.sms) * di.chunk_blocks_per_sm;
+  const int grid = static_cast<int>(work_items < resident ? (work_items > 0 ? work_items : 1) : resident);
+  if (g_prof_start) cudaEventRecord(g_prof_start, stream);
+  chunk_kernel<<<grid, kThreads, kChunkSmemBytes, stream>>>(p, work_items);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (g_prof_stop) cudaEventRecord(g_prof_stop, stream);
+  const int mgrid = p.seg_num;
+  merge_kernel<<<mgrid, kMergeThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+TopkParams base_params(const void* d_input, int seg_num, int k, void* d_out_values,
+                       int* d_out_indices, void* d_workspace, const Layout& L, long long slots) {
+  TopkParams p{};
+  const uintptr_t in = reinterpret_cast<uintptr_t>(d_input);
+  p.base = reinterpret_cast<const uint16_t*>(in & ~static_cast<uintptr_t>(15));
+  p.shift = static_cast<int>((in & 15) / 2);
+  p.seg_num = seg_num;
+  p.k = k;
+  p.groups = groups_for_k(k);
+  p.cap = cap_for_k(k);
+  p.slot_capacity = slots;
+  uint8_t* ws = static_cast<uint8_t*>(d_workspace);
+  p.status = reinterpret_cast<uint32_t*>(ws + L.status);
+  p.seg_thresh = reinterpret_cast<uint32_t*>(ws + L.thresh);
+  p.chunk_start = reinterpret_cast<uint32_t*>(ws + L.chunk_start);
+  p.chunk_count = reinterpret_cast<uint32_t*>(ws + L.counts);
+  p.cand = reinterpret_cast<uint32_t*>(ws + L.cand);
+  p.out_values = static_cast<uint16_t*>(d_out_values);
+  p.out_indices = d_out_indices;
+  return p;
+}
+
+bool pointers_ok(const void* in, const void* ov, const int* oi, const void* ws) {
+  if (!in || !ov || !oi || !ws) return false;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(in), b = reinterpret_cast<uintptr_t>(ov),
+                  c = reinterpret_cast<uintptr_t>(oi), d = reinterpret_cast<uintptr_t>(ws);
+  return (a % 2 == 0) && (b % 2 == 0) && (c % 4 == 0) && (d % 16 == 0);
+}
+
+}  // namespace
+}  // namespace bt
+
+extern "C" {
+
+size_t bt_topk_half_workspace_size(int seg_num, int seg_len, int k) {
+  if (!bt::fixed_shape_ok(seg_num, seg_len, k)) return 0;
+  const long long slots = static_cast<long long>(seg_num) * bt::slots_per_segment(seg_len);
+  return bt::make_layout(seg_num, slots, bt::cap_for_k(k), false).total;
+}
+
+int bt_topk_half(const void* d_input, int seg_num, int seg_len, int k, void* d_output_values,
+                 int* d_output_indices, void* d_workspace, size_t workspace_bytes, void* stream) {
+  if (!bt::fixed_shape_ok(seg_num, seg_len, k)) return cudaErrorInvalidValue;
+  if (!bt::pointers_ok(d_input, d_output_values, d_output_indices, d_workspace)) {
+    return cudaErrorInvalidValue;
+  }
+  const long long p_max = bt::slots_per_segment(seg_len);
+  const long long slots = static_cast<long long>(seg_num) * p_max;
+  const bt::Layout L = bt::make_layout(seg_num, slots, bt::cap_for_k(k), false);
+  if (workspace_bytes < L.total) return cudaErrorInvalidValue;
+  bt::TopkParams p = bt::base_params(d_input, seg_num, k, d_output_values, d_output_indices,
+                                     d_workspace, L, slots);
+  p.seg_len = seg_len;
+  p.offsets = nullptr;
+  p.p_max = static_cast<int>(p_max);
+  return bt::launch_pipeline(p, false, slots, static_cast<cudaStream_t>(stream));
+}
+
+size_t bt_topk_half_segmented_workspace_size(int seg_num, long long max_total_len, int k) {
+  if (!bt::csr_shape_ok(seg_num, max_total_len, k)) return 0;
+  const long long slots = bt::csr_slot_bound(seg_num, max_total_len);
+  return bt::make_layout(seg_num, slots, bt::cap_for_k(k), true).total;
+}
+
+int bt_topk_half_segmented(const void* d_input, const int* d_offsets, int seg_num,
+                           long long max_total_len, int k, void* d_output_values,
+                           int* d_output_indices, void* d_workspace, size_t workspace_bytes,
+                           void* stream) {
+  if (!bt::csr_shape_ok(seg_num, max_total_len, k)) return cudaErrorInvalidValue;
+  if (!d_offsets || reinterpret_cast<uintptr_t>(d_offsets) % 4 != 0) return cudaErrorInvalidValue;
+  if (!bt::pointers_ok(d_input, d_output_values, d_output_indices, d_workspace)) {
+    return cudaErrorInvalidValue;
+  }
+  const long long slots = bt::csr_slot_bound(seg_num, max_total_len);
+  const bt::Layout L = bt::make_layout(seg_num, slots, bt::cap_for_k(k), true);
+  if (workspace_bytes < L.total) return cudaErrorInvalidValue;
+  bt::TopkParams p = bt::base_params(d_input, seg_num, k, d_output_values, d_output_indices,
+                                     d_workspace, L, slots);
+  p.seg_len = 0;
+  p.offsets = d_offsets;
+  p.p_max = 0;
+  return bt::launch_pipeline(p, true, slots, static_cast<cudaStream_t>(stream));
+}
+
+int bt_workspace_status(const void* d_workspace, int seg_num, void* stream, unsigned* stats) {
+  (void)seg_num;
+  if (!d_workspace) return cudaErrorInvalidValue;
+  uint32_t words[16];
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(words, d_workspace, sizeof(words), cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return -static_cast<int>(e);
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return -static_cast<int>(e);
+  if (stats) {
+    for (int i = 0; i < 4; ++i) stats[i] = words[1 + i];
+  }
+  return static_cast<int>(words[0]);
+}
+
+void bt_set_profile_events(void* ev_start, void* ev_stop) {
+  std::lock_guard<std::mutex> lock(bt::g_mu);
+  if (ev_start && ev_stop) {
+    bt::g_prof_start = static_cast<cudaEvent_t>(ev_start);
+    bt::g_prof_stop = static_cast<cudaEvent_t>(ev_stop);
+  } else {
+    bt::g_prof_start = nullptr;
+    bt::g_prof_stop = nullptr;
+  }
+}
+
+const char* bt_error_string(int code) {
+  if (code < 0) return cudaGetErrorString(static_cast<cudaError_t>(-code));
+  switch (code) {
+    case 0: return "success";
+    case cudaErrorInvalidValue: return "invalid argument (shape, pointer, or workspace size)";
+    default: return cudaGetErrorString(static_cast<cudaError_t>(code));
+  }
+}
+
+int bt_version(void) { return bt::kVersion; }
+
+}  // extern "C"

@@ -1,0 +1,263 @@
+// bt_device.cuh -- shared device primitives for the batched fp16 top-k kernels (sm_100a).
+//
+//   * the fp16 descending key codec (reference: include/type_codec.cuh:13-38);
+//   * mbarrier and bulk-copy (cp.async.bulk, no multicast) wrappers with bounded waits;
+//   * block scans, bin search over 256-bin histograms, and aggregated smem histogram adds.
+#pragma once
+
+#include <cstdint>
+
+#include <cuda_fp16.h>
+
+namespace bt {
+
+// ---- geometry and limits -----------------------------------------------------------
+constexpr int kThreads = 256;                         // chunk kernel block size
+constexpr int kWarps = kThreads / 32;
+constexpr int kVecPerThread = 8;                      // 16-byte vectors per thread
+constexpr int kVecPerChunk = kThreads * kVecPerThread;  // 2048 vectors
+constexpr int kChunkElems = kVecPerChunk * 8;         // 16384 fp16 values
+constexpr int kStageBytes = kVecPerChunk * 16;        // 32 KiB per pipeline stage
+constexpr int kStages = 3;
+constexpr int kMaxK = 1024;
+constexpr int kMergeThreads = 256;
+constexpr int kMaxChunksPerSegment = 4097;            // 2^26 values, misaligned start
+constexpr uint32_t kNoThreshold = 0xFFFFu;
+constexpr uint32_t kWaitCap = 1u << 24;               // bounded mbarrier polling
+
+// status word bits (mirrors BT_STATUS_* in include/batch_topk_b200.h)
+constexpr uint32_t kStatusWaitTimeout = 1;
+constexpr uint32_t kStatusBadOffsets = 2;
+constexpr uint32_t kStatusSegmentTooLong = 4;
+constexpr uint32_t kStatusCertifyFailed = 8;
+
+// ---- codec -------------------------------------------------------------------------
+// Descending key: smaller key ranks first.  Any NaN -> 0xFFFF (last); +-0 -> 0x7FFF;
+// otherwise key = bits ^ (sign ? 0x0000 : 0x7FFF), which is ~encode_half_asc.
+__host__ __device__ __forceinline__ uint32_t desc_key(uint32_t bits) {
+  bits &= 0xFFFFu;
+  if ((bits & 0x7C00u) == 0x7C00u && (bits & 0x03FFu) != 0) return 0xFFFFu;
+  if ((bits & 0x7FFFu) == 0) return 0x7FFFu;
+  return (bits & 0x8000u) ? bits : (bits ^ 0x7FFFu);
+}
+
+// fp16 bit pattern of the (non-NaN) value whose key is `key` (+0 for key 0x7FFF).
+__host__ __device__ __forceinline__ uint32_t key_to_bits(uint32_t key) {
+  return key < 0x8000u ? (key ^ 0x7FFFu) : key;
+}
+
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t w) {
+  __half2 h;
+  *reinterpret_cast<uint32_t*>(&h) = w;
+  return h;
+}
+
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// Bit e (e = 0..7, element order) set when element e of the vector is >= v (NaN: never).
+__device__ __forceinline__ uint32_t ge_mask8(const uint4& w, __half2 v2) {
+  const uint32_t m0 = __hge2_mask(u32_as_h2(w.x), v2);
+  const uint32_t m1 = __hge2_mask(u32_as_h2(w.y), v2);
+  const uint32_t m2 = __hge2_mask(u32_as_h2(w.z), v2);
+  const uint32_t m3 = __hge2_mask(u32_as_h2(w.w), v2);
+  const uint32_t x = (m0 & 0x00020001u) | (m1 & 0x00080004u) | (m2 & 0x00200010u) |
+                     (m3 & 0x00800040u);
+  return (x | (x >> 16)) & 0xFFu;
+}
+
+// Replace the halves whose bit is clear in valid8 by a NaN (ignored by __hmax2).
+__device__ __forceinline__ uint32_t nan_fill_word(uint32_t w, uint32_t valid2) {
+  const uint32_t keep = ((valid2 & 1u) ? 0x0000FFFFu : 0u) | ((valid2 & 2u) ? 0xFFFF0000u : 0u);
+  return (w & keep) | (0x7E007E00u & ~keep);
+}
+
+__device__ __forceinline__ uint4 nan_fill(uint4 w, uint32_t valid8) {
+  w.x = nan_fill_word(w.x, valid8);
+  w.y = nan_fill_word(w.y, valid8 >> 2);
+  w.z = nan_fill_word(w.z, valid8 >> 4);
+  w.w = nan_fill_word(w.w, valid8 >> 6);
+  return w;
+}
+
+// 8-bit mask of the elements of aligned vector gv that lie inside [a0, a1).
+__device__ __forceinline__ uint32_t valid_mask8(long long gv, long long a0, long long a1) {
+  const long long e0 = gv * 8;
+  long long lo = a0 - e0;
+  long long hi = a1 - e0;
+  lo = lo < 0 ? 0 : (lo > 8 ? 8 : lo);
+  hi = hi < 0 ? 0 : (hi > 8 ? 8 : hi);
+  if (hi <= lo) return 0u;
+  return ((0xFFu << lo) & (0xFFu >> (8 - hi))) & 0xFFu;
+}
+
+// ---- PTX wrappers: mbarrier + bulk copy ---------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false if the phase did not complete within kWaitCap polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t it = 0; it < kWaitCap; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  return false;
+}
+
+// One bulk global->shared copy (16-byte aligned addresses, size a multiple of 16), completing
+// transaction bytes on `bar`.  No multicast.  Evict-first L2 hint: the input is read once.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+
+// ---- block and warp collectives ----------------------------------------------------
+template <int THREADS>
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* total,
+                                                    uint32_t* warp_tot) {
+  constexpr int NW = THREADS / 32;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  uint32_t pre = 0, tot = 0;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    const uint32_t t = warp_tot[w];
+    pre += (w < warp) ? t : 0u;
+    tot += t;
+  }
+  *total = tot;
+  __syncthreads();
+  return pre + x - v;
+}
+
+// Warp-collective (call from one full warp): first bin b of hist[256] where
+// base + sum(hist[0..b]) >= target.  Lane 0 writes *out_bin (256 when never reached) and
+// *out_before (count before that bin, or the grand total when never reached).
+__device__ __forceinline__ void warp_find_bin(const uint32_t* hist, uint32_t base,
+                                              uint32_t target, int* out_bin,
+                                              uint32_t* out_before) {
+  const int lane = threadIdx.x & 31;
+  const uint4 a = lds128(hist + lane * 8);
+  const uint4 b = lds128(hist + lane * 8 + 4);
+  const uint32_t c[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t tot = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += c[i];
+  uint32_t incl = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const uint32_t excl = incl - tot;
+  const uint32_t grand = __shfl_sync(0xFFFFFFFFu, incl, 31);
+  const unsigned hit = __ballot_sync(0xFFFFFFFFu, base + incl >= target);
+  if (hit == 0) {
+    if (lane == 0) {
+      *out_bin = 256;
+      *out_before = base + grand;
+    }
+    return;
+  }
+  const int L = __ffs(hit) - 1;
+  if (lane == L) {
+    uint32_t run = base + excl;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (run + c[i] >= target) {
+        *out_bin = lane * 8 + i;
+        *out_before = run;
+        break;
+      }
+      run += c[i];
+    }
+  }
+}
+
+// Histogram add of one value per lane, aggregated across equal bins in the warp.
+__device__ __forceinline__ void hist_add_match(uint32_t* hist, uint32_t bin, bool active) {
+  const uint32_t b = active ? bin : 0xFFFFFFFFu;
+  const uint32_t peers = __match_any_sync(0xFFFFFFFFu, b);
+  if (active && (threadIdx.x & 31) == static_cast<unsigned>(__ffs(peers) - 1)) {
+    atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+  }
+}
+
+// Per-thread run-length aggregation of histogram adds (for sequential scans where equal
+// bins cluster, e.g. tie-heavy or sorted data).
+struct RunHist {
+  uint32_t bin = 0xFFFFFFFFu;
+  uint32_t count = 0;
+  __device__ __forceinline__ void add(uint32_t* hist, uint32_t b) {
+    if (b == bin) {
+      ++count;
+      return;
+    }
+    if (count) atomicAdd(&hist[bin], count);
+    bin = b;
+    count = 1;
+  }
+  __device__ __forceinline__ void flush(uint32_t* hist) {
+    if (count) atomicAdd(&hist[bin], count);
+    count = 0;
+    bin = 0xFFFFFFFFu;
+  }
+};
+
+}  // namespace bt

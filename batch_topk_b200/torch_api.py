@@ -1,0 +1,97 @@
+"""Tensor-level helpers over the C ABI (PyTorch provides device memory and streams only).
+
+    values, indices = topk(x, k)                      # x: [seg_num, seg_len] fp16 on CUDA
+    values, indices = topk_segmented(x, offsets, k)   # x: 1-D fp16, offsets: int32 [seg_num+1]
+
+Values come back as fp16 (the input's own bit patterns), indices as int32, both
+[seg_num, k]; descending by value, lower index first among equal values, NaN last.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import (
+    BatchTopkError,
+    batch_topk_half,
+    batch_topk_half_segmented,
+    batch_topk_half_segmented_workspace_size,
+    batch_topk_half_workspace_size,
+)
+
+
+class Workspace:
+    """Grow-only device workspace, one per (device, stream) user."""
+
+    def __init__(self, device=None):
+        self.device = torch.device(device or "cuda")
+        self.buf = None
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() < nbytes:
+            self.buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+_default_ws: dict = {}
+
+
+def _ws(device, ws):
+    if ws is not None:
+        return ws
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    if key not in _default_ws:
+        _default_ws[key] = Workspace(device)
+    return _default_ws[key]
+
+
+def _stream(device, stream):
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    return s.cuda_stream
+
+
+def topk(x: torch.Tensor, k: int, *, workspace: Workspace | None = None, stream=None,
+         out: tuple | None = None):
+    if x.dtype != torch.float16 or x.dim() != 2 or not x.is_cuda:
+        raise ValueError("x must be a 2-D float16 CUDA tensor")
+    x = x.contiguous()
+    seg_num, seg_len = x.shape
+    nbytes = batch_topk_half_workspace_size(seg_num, seg_len, k)
+    if nbytes == 0:
+        raise BatchTopkError(1, f"unsupported shape ({seg_num}, {seg_len}, k={k})")
+    ws = _ws(x.device, workspace).get(nbytes)
+    if out is None:
+        vals = torch.empty((seg_num, k), dtype=torch.float16, device=x.device)
+        idx = torch.empty((seg_num, k), dtype=torch.int32, device=x.device)
+    else:
+        vals, idx = out
+    rc = batch_topk_half(x.data_ptr(), seg_num, seg_len, k, vals.data_ptr(), idx.data_ptr(),
+                         ws.data_ptr(), ws.numel(), _stream(x.device, stream))
+    if rc != 0:
+        raise BatchTopkError(rc, "bt_topk_half")
+    return vals, idx
+
+
+def topk_segmented(x: torch.Tensor, offsets: torch.Tensor, k: int, *,
+                   max_total_len: int | None = None, workspace: Workspace | None = None,
+                   stream=None, out: tuple | None = None):
+    if x.dtype != torch.float16 or x.dim() != 1 or not x.is_cuda:
+        raise ValueError("x must be a 1-D float16 CUDA tensor")
+    if offsets.dtype != torch.int32 or offsets.dim() != 1 or offsets.device != x.device:
+        raise ValueError("offsets must be a 1-D int32 tensor on x's device")
+    seg_num = offsets.numel() - 1
+    total = x.numel() if max_total_len is None else max_total_len
+    nbytes = batch_topk_half_segmented_workspace_size(seg_num, total, k)
+    if nbytes == 0:
+        raise BatchTopkError(1, f"unsupported CSR batch (seg_num={seg_num}, k={k})")
+    ws = _ws(x.device, workspace).get(nbytes)
+    if out is None:
+        vals = torch.empty((seg_num, k), dtype=torch.float16, device=x.device)
+        idx = torch.empty((seg_num, k), dtype=torch.int32, device=x.device)
+    else:
+        vals, idx = out
+    rc = batch_topk_half_segmented(x.data_ptr(), offsets.data_ptr(), seg_num, total, k,
+                                   vals.data_ptr(), idx.data_ptr(), ws.data_ptr(), ws.numel(),
+                                   _stream(x.device, stream))
+    if rc != 0:
+        raise BatchTopkError(rc, "bt_topk_half_segmented")
+    return vals, idx

@@ -1,0 +1,88 @@
+/*
+ * batch_topk_b200.h -- C ABI of the B200 batched fp16 top-k engine.
+ *
+ * Semantics follow fire-emblem/batch_topk (the reference):
+ *   - For each segment, return the top-k values and their segment-local int32 indices.
+ *   - Order: values descending; equal values go to the LOWER index; every NaN ranks below
+ *     every number, -inf included, and NaNs tie among themselves by index; -0 == +0.
+ *     (include/batch_topk_types.cuh:50-92 cpu_reference_topk, :100-113 candidate_better,
+ *      include/type_codec.cuh:13-38.)
+ *   - Output values are the input's own fp16 bit patterns at the returned indices.
+ *   - Outputs are row-major [seg_num, k].  All calls are asynchronous on `stream`; the
+ *     caller owns every buffer.  The workspace needs no initialisation.
+ *
+ * Return values are cudaError_t codes (0 = cudaSuccess, 1 = cudaErrorInvalidValue).
+ * fp16 data is passed as `const void*` (IEEE binary16 bit patterns); `stream` is a
+ * cudaStream_t (NULL = legacy default stream).
+ *
+ * Differences from the reference's limits (deliberate):
+ *   - seg_len up to BT_MAX_SEG_LEN (the reference stops at 10000);
+ *   - k up to BT_MAX_K (the reference stops at 128);
+ *   - a CSR (segment-offsets) entry point, which the reference does not have; on it a
+ *     segment shorter than k is valid: its first len slots hold the result and the rest
+ *     hold value 0xFC00 (-inf) and index -1.
+ */
+#ifndef BATCH_TOPK_B200_H_
+#define BATCH_TOPK_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BT_MAX_K 1024
+#define BT_MAX_SEG_LEN (1 << 26)
+
+/* Replaces radix_topk::batch_topk_half (include/batch_topk.cuh:10-19).  Same arguments and
+ * error contract: cudaErrorInvalidValue for seg_num <= 0, seg_len <= 0, k <= 0, k > seg_len,
+ * k > BT_MAX_K, seg_len > BT_MAX_SEG_LEN, a NULL pointer, or workspace_bytes below
+ * bt_topk_half_workspace_size(seg_num, seg_len, k).  Launch errors are returned as is. */
+int bt_topk_half(const void* d_input, int seg_num, int seg_len, int k, void* d_output_values,
+                 int* d_output_indices, void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces radix_topk::batch_topk_half_workspace_size (include/batch_topk.cuh:21).
+ * Returns 0 for an unsupported shape, as the reference does (src/batch_topk.cu:35-40). */
+size_t bt_topk_half_workspace_size(int seg_num, int seg_len, int k);
+
+/* Variable-length (CSR) batch; no reference counterpart (the reference is fixed-length only,
+ * include/batch_topk.cuh:10-19).  Segment s is d_input[d_offsets[s] .. d_offsets[s+1]);
+ * d_offsets holds seg_num+1 non-decreasing int32 element offsets on the device.
+ * max_total_len bounds d_offsets[seg_num] - d_offsets[0] and sizes the workspace.
+ * Segments shorter than k are valid (padding as described above). */
+int bt_topk_half_segmented(const void* d_input, const int* d_offsets, int seg_num,
+                           long long max_total_len, int k, void* d_output_values,
+                           int* d_output_indices, void* d_workspace, size_t workspace_bytes,
+                           void* stream);
+
+size_t bt_topk_half_segmented_workspace_size(int seg_num, long long max_total_len, int k);
+
+/* Reads back (synchronously, on `stream`) the device status word of the last call that used
+ * this workspace: 0 when every device-side check passed, otherwise a bitwise OR of
+ * BT_STATUS_* flags.  stats (may be NULL) receives 4 counters: chunks that needed the exact
+ * local select, chunks that reused a published threshold, chunks that ran the group-max
+ * select, and segments merged. */
+#define BT_STATUS_OK 0
+#define BT_STATUS_WAIT_TIMEOUT 1    /* a bulk-copy wait hit its iteration cap */
+#define BT_STATUS_BAD_OFFSETS 2     /* CSR offsets decreasing or beyond max_total_len */
+#define BT_STATUS_SEGMENT_TOO_LONG 4
+#define BT_STATUS_CERTIFY_FAILED 8  /* fewer candidates than the threshold certified */
+int bt_workspace_status(const void* d_workspace, int seg_num, void* stream, unsigned* stats);
+
+/* Optional timing hook: when both are non-NULL cudaEvent_t handles, every later call records
+ * ev_start just before its main (streaming) kernel and ev_stop just after it, on the call's
+ * stream.  Pass NULLs to switch it off.  Process-wide; not for concurrent callers. */
+void bt_set_profile_events(void* ev_start, void* ev_stop);
+
+/* Human-readable text for a return code or status flag set. */
+const char* bt_error_string(int code);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int bt_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BATCH_TOPK_B200_H_ */

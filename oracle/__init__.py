@@ -1,0 +1,17 @@
+"""Parity checker for batch_topk_b200 -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py`` (its CPU-baseline and
+``--impl reference`` legs) may import this package.  The product library never does.
+
+* ``topk_oracle.c``   -- C restatement of the reference's CPU top-k and select state.
+* ``ref_oracle.cpp``  -- C ABI over the reference's own header-only CPU implementation,
+                         built in place from the reference tree into ``oracle/_ref``.
+"""
+from .oracle import (  # noqa: F401
+    Oracle,
+    RefOracle,
+    build,
+    encode_desc,
+    load,
+    load_ref,
+)
