@@ -63,9 +63,10 @@ def batch_topk_half_segmented_workspace_size(seg_num: int, max_total_len: int, k
 def workspace_status(d_workspace: int, seg_num: int = 0, stream: int = 0):
     """Synchronously reads the device status of the last call on this workspace.
 
-    Returns (flags, stats) where stats = (exact-select chunks, reused-threshold chunks,
-    group-max selects, merged segments); stats are only counted with BT_STATS=1."""
-    stats = (C.c_uint * 4)()
+    Returns (flags, stats) where stats = (exact-select chunks, chunks with no candidate,
+    group-max selects, rows emitted, verified first-chunk guesses, reserved); stats are only
+    counted with BT_STATS=1."""
+    stats = (C.c_uint * 6)()
     rc = _lib.load().bt_workspace_status(d_workspace, seg_num, stream, C.byref(stats))
     if rc < 0:
         raise BatchTopkError(-rc, "bt_workspace_status")
@@ -75,6 +76,19 @@ def workspace_status(d_workspace: int, seg_num: int = 0, stream: int = 0):
 def set_profile_events(ev_start: int | None, ev_stop: int | None) -> None:
     """Record cudaEvent_t handles around the streaming kernel of later calls (None: off)."""
     _lib.load().bt_set_profile_events(ev_start or None, ev_stop or None)
+
+
+def device_info() -> dict:
+    """SM count, resident blocks per SM and shared memory per block of the top-k kernel."""
+    import ctypes as C
+
+    buf = (C.c_int * 6)()
+    rc = _lib.load().bt_device_info(buf, 6)
+    if rc != 0:
+        raise BatchTopkError(rc, "bt_device_info")
+    keys = ("sms", "blocks_per_sm_small_k", "blocks_per_sm_large_k", "smem_small_k",
+            "smem_large_k", "threads_per_block")
+    return dict(zip(keys, list(buf)))
 
 
 def version() -> int:

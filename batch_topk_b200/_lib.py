@@ -18,6 +18,7 @@ EXPORTED = (
     "bt_topk_half_segmented_workspace_size",
     "bt_workspace_status",
     "bt_set_profile_events",
+    "bt_device_info",
     "bt_error_string",
     "bt_version",
 )
@@ -49,12 +50,14 @@ def load() -> C.CDLL:
         lib.bt_topk_half_segmented.restype = i32
         lib.bt_topk_half_segmented_workspace_size.argtypes = [i32, i64, i32]
         lib.bt_topk_half_segmented_workspace_size.restype = sz
-        lib.bt_workspace_status.argtypes = [vp, i32, vp, C.POINTER(C.c_uint * 4)]
+        lib.bt_workspace_status.argtypes = [vp, i32, vp, C.POINTER(C.c_uint * 6)]
         lib.bt_workspace_status.restype = i32
         lib.bt_set_profile_events.argtypes = [vp, vp]
         lib.bt_set_profile_events.restype = None
         lib.bt_error_string.argtypes = [i32]
         lib.bt_error_string.restype = C.c_char_p
+        lib.bt_device_info.argtypes = [C.POINTER(C.c_int), i32]
+        lib.bt_device_info.restype = i32
         lib.bt_version.argtypes = []
         lib.bt_version.restype = i32
         _lib = lib

@@ -13,7 +13,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 SRC = os.path.join(HERE, "csrc", "batch_topk.cu")
-HEADERS = [os.path.join(HERE, "csrc", f) for f in ("bt_device.cuh", "bt_kernels.cuh")] + [
+HEADERS = [os.path.join(HERE, "csrc", f) for f in ("bt_device.cuh", "bt_kernels.cuh", "bt_small.cuh")] + [
     os.path.join(REPO, "include", "batch_topk_b200.h")
 ]
 LIB_DIR = os.path.join(HERE, "lib")

@@ -36,10 +36,11 @@ long long csr_slot_bound(long long seg_num, long long total_len) {
 }
 
 struct Layout {
-  size_t status, thresh, chunk_start, counts, cand, total;
+  size_t status, thresh, done, chunk_start, counts, offs, cand, total;
 };
 
-// status | seg_thresh | chunk_start (CSR) | chunk_count | candidates, 256-byte aligned.
+// status | seg_thresh | seg_done | chunk_start (CSR) | chunk_count | chunk_off | candidates,
+// each region 256-byte aligned.
 Layout make_layout(long long seg_num, long long slots, int cap, bool csr) {
   Layout L{};
   size_t off = 0;
@@ -50,8 +51,10 @@ Layout make_layout(long long seg_num, long long slots, int cap, bool csr) {
   };
   L.status = take(16 * sizeof(uint32_t));
   L.thresh = take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
+  L.done = take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
   L.chunk_start = csr ? take(static_cast<size_t>(seg_num + 1) * sizeof(uint32_t)) : 0;
   L.counts = take(static_cast<size_t>(slots) * sizeof(uint32_t));
+  L.offs = take(static_cast<size_t>(slots + 1) * sizeof(uint32_t));
   L.cand = take(static_cast<size_t>(slots) * cap * sizeof(uint32_t));
   L.total = off;
   return L;
@@ -70,7 +73,7 @@ bool csr_shape_ok(int seg_num, long long max_total_len, int k) {
 struct DeviceInfo {
   bool ready = false;
   int sms = 0;
-  int chunk_blocks_per_sm = 0;
+  int blocks_per_sm[2] = {0, 0};  // topk_kernel<false>, topk_kernel<true>
 };
 
 std::mutex g_mu;
@@ -86,15 +89,23 @@ cudaError_t device_info(DeviceInfo* out) {
   std::lock_guard<std::mutex> lock(g_mu);
   DeviceInfo& d = g_dev[dev];
   if (!d.ready) {
-    e = cudaFuncSetAttribute(chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kChunkSmemBytes));
+    e = cudaFuncSetAttribute(topk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(SmemLayout<false>::bytes));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(SmemLayout<true>::bytes));
     if (e != cudaSuccess) return e;
     e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.chunk_blocks_per_sm, chunk_kernel,
-                                                      kThreads, kChunkSmemBytes);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.blocks_per_sm[0], topk_kernel<false>,
+                                                      block_threads<false>(),
+                                                      SmemLayout<false>::bytes);
     if (e != cudaSuccess) return e;
-    if (d.chunk_blocks_per_sm < 1) return cudaErrorInvalidConfiguration;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.blocks_per_sm[1], topk_kernel<true>,
+                                                      block_threads<true>(),
+                                                      SmemLayout<true>::bytes);
+    if (e != cudaSuccess) return e;
+    if (d.blocks_per_sm[0] < 1 || d.blocks_per_sm[1] < 1) return cudaErrorInvalidConfiguration;
     if (g_stats < 0) {
       const char* s = std::getenv("BT_STATS");
       g_stats = (s && s[0] == '1') ? 1 : 0;
@@ -110,7 +121,6 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
   cudaError_t e = device_info(&di);
   if (e != cudaSuccess) return e;
   p.stats = g_stats > 0 ? 1 : 0;
-  p.reuse = 1;
   if (csr) {
     csr_prep_kernel<<<1, 1024, 0, stream>>>(p);
   } else {
@@ -119,16 +129,19 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const long long resident = static_cast<long long>(di.sms) * di.chunk_blocks_per_sm;
+  const bool big = p.k > Cfg<false>::kSelCap;
+  const long long resident = static_cast<long long>(di.sms) * di.blocks_per_sm[big ? 1 : 0];
   const int grid = static_cast<int>(work_items < resident ? (work_items > 0 ? work_items : 1) : resident);
   if (g_prof_start) cudaEventRecord(g_prof_start, stream);
-  chunk_kernel<<<grid, kThreads, kChunkSmemBytes, stream>>>(p, work_items);
+  if (big) {
+    topk_kernel<true><<<grid, block_threads<true>(), SmemLayout<true>::bytes, stream>>>(p, work_items);
+  } else {
+    topk_kernel<false><<<grid, block_threads<false>(), SmemLayout<false>::bytes, stream>>>(p, work_items);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (g_prof_stop) cudaEventRecord(g_prof_stop, stream);
-  const int mgrid = p.seg_num;
-  merge_kernel<<<mgrid, kMergeThreads, 0, stream>>>(p);
-  return cudaGetLastError();
+  return cudaSuccess;
 }
 
 TopkParams base_params(const void* d_input, int seg_num, int k, void* d_out_values,
@@ -145,8 +158,10 @@ TopkParams base_params(const void* d_input, int seg_num, int k, void* d_out_valu
   uint8_t* ws = static_cast<uint8_t*>(d_workspace);
   p.status = reinterpret_cast<uint32_t*>(ws + L.status);
   p.seg_thresh = reinterpret_cast<uint32_t*>(ws + L.thresh);
+  p.seg_done = reinterpret_cast<uint32_t*>(ws + L.done);
   p.chunk_start = reinterpret_cast<uint32_t*>(ws + L.chunk_start);
   p.chunk_count = reinterpret_cast<uint32_t*>(ws + L.counts);
+  p.chunk_off = reinterpret_cast<uint32_t*>(ws + L.offs);
   p.cand = reinterpret_cast<uint32_t*>(ws + L.cand);
   p.out_values = static_cast<uint16_t*>(d_out_values);
   p.out_indices = d_out_indices;
@@ -225,7 +240,7 @@ int bt_workspace_status(const void* d_workspace, int seg_num, void* stream, unsi
   e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return -static_cast<int>(e);
   if (stats) {
-    for (int i = 0; i < 4; ++i) stats[i] = words[1 + i];
+    for (int i = 0; i < BT_STATS_WORDS; ++i) stats[i] = words[1 + i];
   }
   return static_cast<int>(words[0]);
 }
@@ -248,6 +263,17 @@ const char* bt_error_string(int code) {
     case cudaErrorInvalidValue: return "invalid argument (shape, pointer, or workspace size)";
     default: return cudaGetErrorString(static_cast<cudaError_t>(code));
   }
+}
+
+int bt_device_info(int* info, int n) {
+  bt::DeviceInfo di;
+  const cudaError_t e = bt::device_info(&di);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const int v[6] = {di.sms, di.blocks_per_sm[0], di.blocks_per_sm[1],
+                    static_cast<int>(bt::SmemLayout<false>::bytes),
+                    static_cast<int>(bt::SmemLayout<true>::bytes), bt::block_threads<false>()};
+  for (int i = 0; i < n && i < 6; ++i) info[i] = v[i];
+  return 0;
 }
 
 int bt_version(void) { return bt::kVersion; }

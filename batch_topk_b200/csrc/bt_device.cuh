@@ -22,7 +22,8 @@ constexpr int kStages = 3;
 constexpr int kMaxK = 1024;
 constexpr int kMergeThreads = 256;
 constexpr int kMaxChunksPerSegment = 4097;            // 2^26 values, misaligned start
-constexpr uint32_t kNoThreshold = 0xFFFFu;
+constexpr uint32_t kNoThreshold = 0xFFFFu;  // key bound that admits every value, NaN too
+constexpr uint32_t kFewerThanK = 0x10000u;  // "fewer than k candidates": all of them qualify
 constexpr uint32_t kWaitCap = 1u << 24;               // bounded mbarrier polling
 
 // status word bits (mirrors BT_STATUS_* in include/batch_topk_b200.h)
@@ -60,6 +61,17 @@ __device__ __forceinline__ uint32_t ge_mask8(const uint4& w, __half2 v2) {
   const uint32_t m1 = __hge2_mask(u32_as_h2(w.y), v2);
   const uint32_t m2 = __hge2_mask(u32_as_h2(w.z), v2);
   const uint32_t m3 = __hge2_mask(u32_as_h2(w.w), v2);
+  const uint32_t x = (m0 & 0x00020001u) | (m1 & 0x00080004u) | (m2 & 0x00200010u) |
+                     (m3 & 0x00800040u);
+  return (x | (x >> 16)) & 0xFFu;
+}
+
+// Bit e set when element e is > v (NaN: never).
+__device__ __forceinline__ uint32_t gt_mask8(const uint4& w, __half2 v2) {
+  const uint32_t m0 = __hgt2_mask(u32_as_h2(w.x), v2);
+  const uint32_t m1 = __hgt2_mask(u32_as_h2(w.y), v2);
+  const uint32_t m2 = __hgt2_mask(u32_as_h2(w.z), v2);
+  const uint32_t m3 = __hgt2_mask(u32_as_h2(w.w), v2);
   const uint32_t x = (m0 & 0x00020001u) | (m1 & 0x00080004u) | (m2 & 0x00200010u) |
                      (m3 & 0x00800040u);
   return (x | (x >> 16)) & 0xFFu;
@@ -160,7 +172,31 @@ __device__ __forceinline__ uint4 lds128(const void* p) {
 }
 
 // ---- block and warp collectives ----------------------------------------------------
+// Named barrier 1 over the first THREADS threads of the block (the consumer warps of a
+// warp-specialised kernel; the producer warp never joins it).
 template <int THREADS>
+__device__ __forceinline__ void group_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(THREADS) : "memory");
+}
+
+// OR-reduction of a predicate over the same group, returned to every member.
+template <int THREADS>
+__device__ __forceinline__ bool group_or(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "n"(THREADS)
+      : "memory");
+  return r != 0;
+}
+
+// Exclusive scan over the THREADS threads that call it; synchronises with group_sync when
+// GROUP is true (warp-specialised kernels) and __syncthreads otherwise.
+template <int THREADS, bool GROUP = false>
 __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* total,
                                                     uint32_t* warp_tot) {
   constexpr int NW = THREADS / 32;
@@ -173,7 +209,7 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* total,
     if (lane >= o) x += y;
   }
   if (lane == 31) warp_tot[warp] = x;
-  __syncthreads();
+  if (GROUP) group_sync<THREADS>(); else __syncthreads();
   uint32_t pre = 0, tot = 0;
 #pragma unroll
   for (int w = 0; w < NW; ++w) {
@@ -182,7 +218,7 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* total,
     tot += t;
   }
   *total = tot;
-  __syncthreads();
+  if (GROUP) group_sync<THREADS>(); else __syncthreads();
   return pre + x - v;
 }
 

@@ -1,27 +1,36 @@
 // bt_kernels.cuh -- the batched fp16 top-k pipeline for sm_100a.
 //
-// One streaming pass over HBM replaces the reference's three full reads
-// (src/radix_histogram.cuh K1/K2 and src/candidate_compact.cuh K9):
+// One streaming pass over HBM replaces the reference's three full reads (the high-byte and
+// low-byte histograms, src/radix_histogram.cuh, and the compaction,
+// src/candidate_compact.cuh):
 //
-//  chunk_kernel (persistent, 2 CTAs/SM, 3-stage cp.async.bulk pipeline of 32 KiB chunks)
-//    For each chunk of a segment (<= 16384 values):
-//      1. certified threshold: the k-th best of the chunk's group maxima.  Each maximum
-//         is a distinct element, so at least k elements of the chunk are >= it, and every
-//         member of the segment's top-k is >= it.  The chunk publishes it with atomicMin on
-//         the segment's descending key; later chunks try the published value first.
-//      2. ordered compaction: values >= threshold are written, in index order, to the
-//         chunk's candidate slot (fp16 bits << 16 | chunk-local index).  Ballot-free: an
-//         8-bit half2 compare mask per 16-byte vector, popc, one block exclusive scan.
-//      3. if more than `cap` candidates survive, an exact local select (two 8-bit digit
-//         passes over smem, the reference's radix_boundary_select logic) keeps exactly the
-//         chunk's k best, lowest index first among ties.
-//  merge_kernel (one CTA per segment)
-//    Concatenates the segment's chunk lists (index order), drops entries worse than the
-//    segment's final threshold, finds the exact cutoff key with two 8-bit digit passes,
-//    keeps keys below the cutoff plus the first ties by index, and bitonic-sorts those <= k
-//    entries by (key, index).  This is the reference's boundary select + compaction + final
-//    sort (src/radix_boundary_select.cuh, src/candidate_compact.cuh, src/final_topk50.cuh)
-//    applied to a few hundred candidates instead of the whole segment.
+// topk_kernel: persistent, 2 CTAs per SM, warp-specialised.
+//   * Producer warp (one elected lane): walks the CTA's contiguous range of chunk work items
+//     (segment-major) and streams each chunk (<= 16384 fp16 values, 32 KiB) into a shared
+//     memory stage with one cp.async.bulk (no multicast), signalling a "full" mbarrier.
+//   * 8 consumer warps, per chunk:
+//       1. threshold: on the first chunk of a segment (or when too many values survive), the
+//          k-th best of the chunk's group maxima.  Each maximum is a distinct element, so at
+//          least k elements of the chunk are >= it and every member of the segment's top-k
+//          is >= it (a certified bound; no histogram of the whole chunk is needed).
+//       2. ordered compaction: values passing the threshold are written in index order to
+//          the chunk's candidate slot as (fp16 bits << 16 | chunk-local index), from an 8-bit
+//          half2 compare mask per 16-byte vector and one exclusive scan over the block.
+//       3. after a chunk has written >= k candidates with key <= K, every later chunk of the
+//          segment in this CTA has larger indices, so it only needs keys strictly below K:
+//          ties at K can no longer win.  This keeps tie-heavy rows (all values equal, a few
+//          hundred copies of the maximum) to about k candidates per segment.
+//       4. more than `cap` survivors: an exact local select (two 8-bit digit passes, the
+//          reference's radix_boundary_select logic) keeps exactly the chunk's k best.
+//     then release the stage on an "empty" mbarrier.
+//   * When the CTA finishes its part of a segment, the last CTA to finish (per-segment
+//     arrival counter; usually the only one) merges the segment: concatenates the chunk lists
+//     in index order, drops keys above the final threshold, finds the exact cutoff key with
+//     two 8-bit digit passes, keeps keys below it plus the first ties by index, and places
+//     each survivor at its rank by (key, index).  This is the reference's boundary select,
+//     compaction and final sort (src/radix_boundary_select.cuh, src/candidate_compact.cuh,
+//     src/final_topk50.cuh, src/final_block_sort.cuh) on ~k candidates, while the producer
+//     keeps prefetching the next chunks.
 #pragma once
 
 #include <cstddef>
@@ -43,10 +52,11 @@ struct TopkParams {
   int k;
   int groups;                    // group maxima per thread in the threshold select
   int cap;                       // candidate capacity per chunk slot
-  int reuse;                     // try the published segment threshold first
   int stats;                     // count events into status[1..4]
-  uint32_t* seg_thresh;          // [seg_num]
+  uint32_t* seg_thresh;          // [seg_num] thresholds shared by CTAs splitting a segment
+  uint32_t* seg_done;            // [seg_num] chunks finished (arrival counter)
   uint32_t* chunk_count;         // [slot_capacity]
+  uint32_t* chunk_off;           // [slot_capacity] merge scratch for very long segments
   uint32_t* cand;                // [slot_capacity * cap]
   uint32_t* status;              // [16]
   uint16_t* out_values;          // [seg_num * k]
@@ -81,216 +91,462 @@ __device__ __forceinline__ SegGeom seg_geom(const TopkParams& p, int s) {
   return g;
 }
 
+// Small k keeps three 32 KiB load stages; large k gives one up for a bigger merge buffer.
+template <bool BIG>
+struct Cfg {
+  static constexpr int kStagesN = BIG ? 2 : 3;
+  static constexpr int kSelCap = BIG ? kMaxK : 128;      // >= k
+  static constexpr int kCacheCap = BIG ? 2048 : 1024;    // merge cache, 64-bit composites
+  static constexpr int kCoffCap = 128;                   // chunks per segment in smem
+  static constexpr int kGroupWords = BIG ? 4 : 1;        // packed group-max key words/thread
+};
+
 struct StageInfo {
   long long cv0;   // first aligned vector of the chunk
   long long a0, a1;
   long long slot;
-  int s;
-  int nvc;         // vectors in the chunk; 0 = nothing to do
-  uint32_t g_prev; // the segment's published threshold when the load was issued
-  int pad;
+  long long v0;    // first aligned vector of the segment
+  int s, c;
+  int nvc;         // vectors in the chunk; 0 = empty work item
+  int nchunks;     // chunks of the segment
+  int chunk_vecs;
+  int vlo, vhi;    // chunk-relative vectors that straddle the segment ends (-1: none)
+  int last;        // last chunk of this segment in this block's range
 };
 
-struct alignas(16) ChunkSmem {
+template <bool BIG>
+struct alignas(16) Scratch {
   uint32_t hist1[256];  // 16-byte aligned: warp_find_bin reads it with 128-bit loads
   uint32_t hist2[256];
+  unsigned long long cache[Cfg<BIG>::kCacheCap];
+  unsigned long long sel[Cfg<BIG>::kSelCap];
+  alignas(16) uint32_t gkeys[Cfg<BIG>::kGroupWords * kThreads];  // 128-bit reads
+  uint32_t coff[Cfg<BIG>::kCoffCap + 1];
   uint32_t warp_tot[kWarps];
+  uint32_t wcnt[2][kWarps];  // per-warp candidate counts, double-buffered by chunk parity
   int bin1, bin2;
   uint32_t before1, before2;
+  uint32_t bcast[4];
+  uint32_t fail;
 };
 
-// Dynamic shared memory: [stages | ChunkSmem | mbarriers | StageInfo].
-constexpr size_t kSmemOffScratch = static_cast<size_t>(kStages) * kStageBytes;
-constexpr size_t kSmemOffBars = kSmemOffScratch + sizeof(ChunkSmem);
-constexpr size_t kSmemOffInfo = kSmemOffBars + kStages * sizeof(uint64_t);
-constexpr size_t kChunkSmemBytes = kSmemOffInfo + kStages * sizeof(StageInfo);
-static_assert(kSmemOffScratch % 16 == 0 && sizeof(ChunkSmem) % 16 == 0, "hist alignment");
-static_assert(kSmemOffBars % 8 == 0 && kSmemOffInfo % 8 == 0, "mbarrier/info alignment");
+// k <= 128: per-segment state lives with the merger warp (bt_small.cuh).
+constexpr int kBatchCap = 512;  // >= cap for k <= 128 (max(4k, 256))
 
-// Processing order of chunk work items.  Fixed-length rows go chunk-major (all segments'
-// chunk 0, then chunk 1, ...) so later chunks find a published threshold.  CSR batches go
-// in slot order.
-__device__ __forceinline__ void decode_work(const TopkParams& p, long long q, int* s, int* c,
-                                            long long* slot) {
-  if (!p.offsets) {
-    *c = static_cast<int>(q / p.seg_num);
-    *s = static_cast<int>(q % p.seg_num);
-    *slot = static_cast<long long>(*s) * p.p_max + *c;
-  } else {
-    int lo = 0, hi = p.seg_num;  // chunk_start[lo] <= q < chunk_start[hi]
+struct BatchMeta {
+  long long len;        // segment length (values)
+  long long part_slot;  // slot of the first chunk of this block's part of the segment
+  long long seg_slot;   // slot of the segment's chunk 0
+  int s;
+  uint32_t n;           // candidates in the batch
+  int flags;            // kBatchEnd | kBatchStop
+  int mycnt;            // chunks of the segment in this block's part, up to this batch
+  int nchunks;
+  uint32_t K;           // consumers' threshold for the segment
+};
+constexpr int kBatchEnd = 1;
+constexpr int kBatchStop = 2;
+
+template <>
+struct alignas(16) Scratch<false> {
+  uint32_t hist1[256];  // 16-byte aligned: warp_find_bin reads it with 128-bit loads
+  uint32_t hist2[256];
+  unsigned long long batch[2][kBatchCap];  // consumer -> merger candidate batches
+  BatchMeta meta[2];
+  uint64_t batch_full[2];                  // mbarriers: one arrival per consumer warp
+  uint64_t batch_free[2];                  // mbarriers: one arrival by the merger
+  unsigned long long kpub;                 // merger: (segment << 32) | k-th key
+  alignas(16) uint32_t gkeys[Cfg<false>::kGroupWords * kThreads];  // 128-bit reads
+  uint32_t warp_tot[kWarps];
+  uint32_t wcnt[2][kWarps];
+  uint32_t kuse[2];
+  int bin1, bin2;
+  uint32_t before1, before2;
+  uint32_t bcast[4];
+  uint32_t fail;
+};
+using SmallScratch = Scratch<false>;
+
+// Every array read with 128-bit shared loads (lds128) must start on a 16-byte boundary.
+static_assert(offsetof(Scratch<false>, hist1) % 16 == 0 && offsetof(Scratch<false>, hist2) % 16 == 0 &&
+              offsetof(Scratch<false>, gkeys) % 16 == 0, "16-byte alignment of lds128 operands");
+static_assert(offsetof(Scratch<true>, hist1) % 16 == 0 && offsetof(Scratch<true>, hist2) % 16 == 0 &&
+              offsetof(Scratch<true>, gkeys) % 16 == 0, "16-byte alignment of lds128 operands");
+
+// Dynamic shared memory: [stages | Scratch | full[] | empty[] | StageInfo[]].
+template <bool BIG>
+struct SmemLayout {
+  static constexpr int S = Cfg<BIG>::kStagesN;
+  static constexpr size_t off_scratch = static_cast<size_t>(S) * kStageBytes;
+  static constexpr size_t off_full = off_scratch + sizeof(Scratch<BIG>);
+  static constexpr size_t off_empty = off_full + S * sizeof(uint64_t);
+  static constexpr size_t off_info = off_empty + S * sizeof(uint64_t);
+  static constexpr size_t bytes = off_info + S * sizeof(StageInfo);
+  static_assert(off_scratch % 16 == 0 && sizeof(Scratch<BIG>) % 16 == 0, "scratch alignment");
+  static_assert(off_full % 8 == 0 && off_info % 8 == 0, "mbarrier/info alignment");
+};
+
+// k > 128: 8 consumer warps + 1 producer warp.  k <= 128: plus 1 merger warp.
+template <bool BIG>
+constexpr int block_threads() { return BIG ? kThreads + 32 : kThreads + 64; }
+
+__device__ __forceinline__ void csync() { group_sync<kThreads>(); }
+
+// ---- producer ------------------------------------------------------------------------
+
+template <bool BIG>
+__device__ void producer_loop(const TopkParams& p, long long q0, long long q1, uint8_t* stages,
+                              uint64_t* full, uint64_t* empty, StageInfo* info) {
+  constexpr int S = Cfg<BIG>::kStagesN;
+  const uint64_t policy = policy_evict_first();
+  int s = -1;
+  SegGeom g{};
+  long long slot0 = 0;
+  int cs = 0;  // CSR: segment cursor
+  if (p.offsets && q0 < q1) {
+    int lo = 0, hi = p.seg_num;  // chunk_start[lo] <= q0 < chunk_start[hi]
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
-      if (static_cast<long long>(p.chunk_start[mid]) <= q) lo = mid; else hi = mid;
+      if (static_cast<long long>(p.chunk_start[mid]) <= q0) lo = mid; else hi = mid;
     }
-    *s = lo;
-    *c = static_cast<int>(q - p.chunk_start[lo]);
-    *slot = q;
+    cs = lo;
+  }
+  long long issued = 0;
+  for (long long q = q0; q < q1; ++q, ++issued) {
+    const int st = static_cast<int>(issued % S);
+    if (issued >= S) {
+      if (!mbar_wait(&empty[st], static_cast<uint32_t>(((issued / S) - 1) & 1))) {
+        atomicOr(&p.status[0], kStatusWaitTimeout);
+        break;
+      }
+    }
+    int sn, c;
+    if (!p.offsets) {
+      sn = static_cast<int>(q / p.p_max);
+      c = static_cast<int>(q - static_cast<long long>(sn) * p.p_max);
+    } else {
+      while (cs + 1 < p.seg_num && static_cast<long long>(p.chunk_start[cs + 1]) <= q) ++cs;
+      sn = cs;
+      c = static_cast<int>(q - p.chunk_start[cs]);
+    }
+    if (sn != s) {
+      s = sn;
+      g = seg_geom(p, s);
+      slot0 = q - c;
+    }
+    StageInfo si;
+    si.s = s;
+    si.c = c;
+    si.slot = slot0 + c;
+    si.a0 = g.a0;
+    si.a1 = g.a1;
+    si.v0 = g.v0;
+    si.nchunks = g.nchunks;
+    si.chunk_vecs = g.chunk_vecs;
+    si.last = (c == g.nchunks - 1 || q + 1 == q1) ? 1 : 0;
+    if (c >= g.nchunks) {
+      si.nvc = 0;
+      si.cv0 = 0;
+      si.vlo = si.vhi = -1;
+    } else {
+      si.cv0 = g.v0 + static_cast<long long>(c) * g.chunk_vecs;
+      const long long rem = g.v0 + g.nv - si.cv0;
+      si.nvc = static_cast<int>(rem < g.chunk_vecs ? rem : g.chunk_vecs);
+      const long long first = g.v0 - si.cv0;
+      const long long last = ((g.a1 - 1) >> 3) - si.cv0;
+      si.vlo = ((g.a0 & 7) && first >= 0 && first < si.nvc) ? static_cast<int>(first) : -1;
+      si.vhi = ((g.a1 & 7) && last >= 0 && last < si.nvc) ? static_cast<int>(last) : -1;
+    }
+    info[st] = si;
+    if (si.nvc > 0) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(si.nvc) * 16u);
+      bulk_load(stages + static_cast<size_t>(st) * kStageBytes, p.base + si.cv0 * 8,
+                static_cast<uint32_t>(si.nvc) * 16u, &full[st], policy);
+    } else {
+      mbar_arrive(&full[st]);
+    }
+  }
+  // Do not retire while a bulk copy may still land in this block's shared memory.
+  for (long long r = issued - S; r < issued; ++r) {
+    if (r < 0) continue;
+    mbar_wait(&full[r % S], static_cast<uint32_t>((r / S) & 1));
   }
 }
 
-// Issued by one thread: fills the stage's info and starts its bulk load.
-__device__ __forceinline__ void issue_chunk(const TopkParams& p, long long q, StageInfo* info,
-                                            uint8_t* buf, uint64_t* bar, uint64_t policy) {
-  int s, c;
-  long long slot;
-  decode_work(p, q, &s, &c, &slot);
-  const SegGeom g = seg_geom(p, s);
-  StageInfo si;
-  si.s = s;
-  si.slot = slot;
-  si.a0 = g.a0;
-  si.a1 = g.a1;
-  si.pad = 0;
-  if (c >= g.nchunks) {
-    si.nvc = 0;
-    si.cv0 = 0;
-  } else {
-    si.cv0 = g.v0 + static_cast<long long>(c) * g.chunk_vecs;
-    const long long rem = g.v0 + g.nv - si.cv0;
-    si.nvc = static_cast<int>(rem < g.chunk_vecs ? rem : g.chunk_vecs);
-  }
-  si.g_prev = si.nvc > 0 ? __ldcg(&p.seg_thresh[s]) : kNoThreshold;
-  *info = si;
-  if (si.nvc > 0) {
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(si.nvc) * 16u);
-    bulk_load(buf, p.base + si.cv0 * 8, static_cast<uint32_t>(si.nvc) * 16u, bar, policy);
-  } else {
-    mbar_arrive(bar);
-  }
+// ---- consumer: per-chunk work ---------------------------------------------------------
+
+// A consumer warp is done with a stage: one arrival per warp, after all its lanes.
+__device__ __forceinline__ void release_stage(uint64_t* empty) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(empty);
+}
+
+struct SegState {
+  int s = -1;
+  uint32_t K = kNoThreshold;  // current threshold key (desc)
+  bool strict = false;        // later chunks need key < K
+  bool spilled = false;       // the shared-memory candidate buffer overflowed
+  int mycnt = 0;              // chunks of this segment processed here
+  int nchunks = 0;
+  int chunk_vecs = 0;
+  uint32_t nbuf = 0;          // candidates of this segment in sm.cache
+  uint32_t added = 0;         // candidates added since the threshold was last tightened
+  long long slot0 = 0, v0 = 0, a0 = 0, a1 = 0;
+};
+
+__device__ __forceinline__ uint4 masked_vec(const StageInfo& si, const uint8_t* buf, int vi,
+                                            bool* partial, uint32_t* valid) {
+  const uint4 w = lds128(buf + vi * 16);
+  *partial = (vi == si.vlo) || (vi == si.vhi);
+  *valid = *partial ? valid_mask8(si.cv0 + vi, si.a0, si.a1) : 0xFFu;
+  return w;
 }
 
 // k-th best group maximum of the chunk (descending key), or kNoThreshold when the chunk has
-// fewer than k non-NaN maxima.  Publishes it on the segment.  Block-uniform result.
+// fewer than k non-NaN maxima.  One barrier: every warp then finds the k-th smallest of the
+// group keys itself, by binary search on the key value with warp-wide counts.
+template <bool BIG>
 __device__ uint32_t chunk_select(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
-                                 ChunkSmem& sm) {
+                                 Scratch<BIG>& sm) {
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
   uint32_t acc0 = 0x7E007E00u, acc1 = 0x7E007E00u, acc2 = 0x7E007E00u, acc3 = 0x7E007E00u;
 #pragma unroll
   for (int j = 0; j < kVecPerThread; ++j) {
-    const int vi = j * kThreads + tid;  // strided groups: 8 values kThreads vectors apart
+    const int vi = j * kThreads + tid;  // strided groups: values 2048 apart
     if (vi < si.nvc) {
-      uint4 w = lds128(buf + vi * 16);
-      const long long gv = si.cv0 + vi;
-      if (gv * 8 < si.a0 || gv * 8 + 8 > si.a1) w = nan_fill(w, valid_mask8(gv, si.a0, si.a1));
+      bool partial;
+      uint32_t valid;
+      uint4 w = masked_vec(si, buf, vi, &partial, &valid);
+      if (partial) w = nan_fill(w, valid);
       acc0 = h2_as_u32(__hmax2(u32_as_h2(acc0), u32_as_h2(w.x)));
       acc1 = h2_as_u32(__hmax2(u32_as_h2(acc1), u32_as_h2(w.y)));
       acc2 = h2_as_u32(__hmax2(u32_as_h2(acc2), u32_as_h2(w.z)));
       acc3 = h2_as_u32(__hmax2(u32_as_h2(acc3), u32_as_h2(w.w)));
     }
   }
-  uint32_t keys[8];
-  int ng;
-  if (p.groups >= 8) {
-    keys[0] = desc_key(acc0); keys[1] = desc_key(acc0 >> 16);
-    keys[2] = desc_key(acc1); keys[3] = desc_key(acc1 >> 16);
-    keys[4] = desc_key(acc2); keys[5] = desc_key(acc2 >> 16);
-    keys[6] = desc_key(acc3); keys[7] = desc_key(acc3 >> 16);
-    ng = 8;
+  // group keys, packed two per 32-bit word: ng = 2 * nw keys per thread
+  uint32_t kw[4];
+  int nw;
+  if (BIG && p.groups >= 8) {
+    kw[0] = desc_key(acc0) | (desc_key(acc0 >> 16) << 16);
+    kw[1] = desc_key(acc1) | (desc_key(acc1 >> 16) << 16);
+    kw[2] = desc_key(acc2) | (desc_key(acc2 >> 16) << 16);
+    kw[3] = desc_key(acc3) | (desc_key(acc3 >> 16) << 16);
+    nw = 4;
   } else {
     const uint32_t m0 = h2_as_u32(__hmax2(u32_as_h2(acc0), u32_as_h2(acc2)));
     const uint32_t m1 = h2_as_u32(__hmax2(u32_as_h2(acc1), u32_as_h2(acc3)));
-    if (p.groups == 4) {
-      keys[0] = desc_key(m0); keys[1] = desc_key(m0 >> 16);
-      keys[2] = desc_key(m1); keys[3] = desc_key(m1 >> 16);
-      ng = 4;
+    if (BIG && p.groups == 4) {
+      kw[0] = desc_key(m0) | (desc_key(m0 >> 16) << 16);
+      kw[1] = desc_key(m1) | (desc_key(m1 >> 16) << 16);
+      nw = 2;
     } else {
       const uint32_t m = h2_as_u32(__hmax2(u32_as_h2(m0), u32_as_h2(m1)));
       if (p.groups == 2) {
-        keys[0] = desc_key(m); keys[1] = desc_key(m >> 16);
-        ng = 2;
-      } else {
+        kw[0] = desc_key(m) | (desc_key(m >> 16) << 16);
+      } else {  // one maximum per thread; the pad key 0xFFFF never counts below a threshold
         const __half2 mh = u32_as_h2(m);
         const __half top = __hmax(__low2half(mh), __high2half(mh));
-        keys[0] = desc_key(*reinterpret_cast<const uint16_t*>(&top));
-        ng = 1;
+        kw[0] = desc_key(*reinterpret_cast<const uint16_t*>(&top)) | 0xFFFF0000u;
+      }
+      nw = 1;
+    }
+  }
+  for (int i = 0; i < nw; ++i) sm.gkeys[i * kThreads + tid] = kw[i];
+  csync();
+  // lane l owns words [l * per, (l + 1) * per) of the nw * kThreads words
+  const int per = nw * kThreads / 32;
+  const uint32_t* src = sm.gkeys + lane * per;
+  uint32_t lo = 0, hi = 0xFFFFu;
+  const uint32_t k = static_cast<uint32_t>(p.k);
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi) >> 1;
+    uint32_t cnt = 0;
+    for (int i = 0; i < per; i += 4) {
+      const uint4 w = lds128(src + i);
+      cnt += ((w.x & 0xFFFFu) <= mid) + ((w.x >> 16) <= mid) + ((w.y & 0xFFFFu) <= mid) +
+             ((w.y >> 16) <= mid) + ((w.z & 0xFFFFu) <= mid) + ((w.z >> 16) <= mid) +
+             ((w.w & 0xFFFFu) <= mid) + ((w.w >> 16) <= mid);
+    }
+    if (__reduce_add_sync(0xFFFFFFFFu, cnt) >= k) hi = mid; else lo = mid + 1;
+  }
+  if (tid == 0 && p.stats) atomicAdd(&p.status[3], 1u);
+  return lo;  // 0xFFFF: no certified threshold (fewer than k non-NaN maxima)
+}
+
+// Threshold test of one 16-byte vector: 8-bit element mask (bit e = element e) of values
+// passing `key < K` (STRICT) or `key <= K`, i.e. value > V or value >= V (never NaN).
+template <bool STRICT>
+__device__ __forceinline__ uint32_t pass_mask8(const uint4& w, __half2 v2) {
+  return STRICT ? gt_mask8(w, v2) : ge_mask8(w, v2);
+}
+
+// Is any half of the vector passing?  (OR of the four compares, no compression.)
+template <bool STRICT>
+__device__ __forceinline__ bool pass_any(const uint4& w, __half2 v2) {
+  if (STRICT) {
+    return (__hgt2_mask(u32_as_h2(w.x), v2) | __hgt2_mask(u32_as_h2(w.y), v2) |
+            __hgt2_mask(u32_as_h2(w.z), v2) | __hgt2_mask(u32_as_h2(w.w), v2)) != 0;
+  }
+  return (__hge2_mask(u32_as_h2(w.x), v2) | __hge2_mask(u32_as_h2(w.y), v2) |
+          __hge2_mask(u32_as_h2(w.z), v2) | __hge2_mask(u32_as_h2(w.w), v2)) != 0;
+}
+
+// This thread's 8 vectors (tid*8 .. tid*8+7): exact candidate mask of vector j, with the
+// segment-boundary and take-all (no threshold yet) cases.
+template <bool STRICT>
+__device__ __forceinline__ uint32_t vec_mask(const StageInfo& si, const uint8_t* buf, int vi,
+                                             __half2 v2, bool take_all) {
+  const uint4 w = lds128(buf + vi * 16);
+  uint32_t m = take_all ? 0xFFu : pass_mask8<STRICT>(w, v2);
+  if (vi == si.vlo || vi == si.vhi) m &= valid_mask8(si.cv0 + vi, si.a0, si.a1);
+  return m;
+}
+
+// Flags (bit j: vector tid*8+j holds a candidate) and the exact candidate count of this
+// thread.  The common case costs one 128-bit smem load, four half2 compares and an OR per
+// vector; exact counting only runs on the rare vectors that pass.
+template <bool STRICT>
+__device__ __forceinline__ uint32_t thread_flags(const StageInfo& si, const uint8_t* buf,
+                                                 __half2 v2, bool take_all, uint32_t* count) {
+  const int tid = threadIdx.x;
+  const int vbase = tid * kVecPerThread;
+  const int sw = tid & 7;
+  const bool edge = take_all || (si.vlo >= vbase && si.vlo < vbase + kVecPerThread) ||
+                    (si.vhi >= vbase && si.vhi < vbase + kVecPerThread);
+  uint32_t flags = 0, cnt = 0;
+  if (!edge) {
+#pragma unroll
+    for (int jj = 0; jj < kVecPerThread; ++jj) {
+      const int j = jj ^ sw;  // rotated read order: conflict-free 16-byte smem reads
+      const int vi = vbase + j;
+      if (vi < si.nvc) {
+        const uint4 w = lds128(buf + vi * 16);
+        if (pass_any<STRICT>(w, v2)) {
+          flags |= 1u << j;
+          cnt += __popc(pass_mask8<STRICT>(w, v2));
+        }
+      }
+    }
+  } else {
+    for (int j = 0; j < kVecPerThread; ++j) {
+      const int vi = vbase + j;
+      if (vi < si.nvc) {
+        const uint32_t m = vec_mask<STRICT>(si, buf, vi, v2, take_all);
+        if (m) {
+          flags |= 1u << j;
+          cnt += __popc(m);
+        }
       }
     }
   }
-  // round 1: high byte
-  for (int i = 0; i < ng; ++i) hist_add_match(sm.hist1, keys[i] >> 8, true);
-  __syncthreads();
-  if (tid < 32) warp_find_bin(sm.hist1, 0, p.k, &sm.bin1, &sm.before1);
-  __syncthreads();
-  const int b1 = sm.bin1;
-  uint32_t kc = kNoThreshold;
-  if (b1 < 255) {
-    // round 2: low byte inside the boundary bin
-    for (int i = 0; i < ng; ++i) {
-      hist_add_match(sm.hist2, keys[i] & 0xFFu, (keys[i] >> 8) == static_cast<uint32_t>(b1));
-    }
-    __syncthreads();
-    if (tid < 32) warp_find_bin(sm.hist2, sm.before1, p.k, &sm.bin2, &sm.before2);
-    __syncthreads();
-    kc = (static_cast<uint32_t>(b1) << 8) | static_cast<uint32_t>(sm.bin2);
-  }
-  if (tid == 0) {
-    if (kc < si.g_prev) atomicMin(&p.seg_thresh[si.s], kc);
-    if (p.stats) atomicAdd(&p.status[3], 1u);
-  }
-  sm.hist1[tid] = 0;
-  sm.hist2[tid] = 0;
-  return kc;
+  *count = cnt;
+  return flags;
 }
 
-// 64-bit mask of this thread's candidates: bit 8*j+e for element e of vector tid*8+j.
-__device__ __forceinline__ uint64_t candidate_mask(const StageInfo& si, const uint8_t* buf,
-                                                   uint32_t kuse) {
+__device__ __forceinline__ unsigned long long make_composite(uint32_t word, long long chunk_elem0,
+                                                             long long a0) {
+  const uint32_t raw = word >> 16;
+  const long long idx = chunk_elem0 + (word & 0xFFFFu) - a0;
+  return (static_cast<unsigned long long>(desc_key(raw)) << 48) |
+         (static_cast<unsigned long long>(idx) << 16) | raw;
+}
+
+// Writes this thread's candidates (flagged vectors, index order) at [base, ...) of the
+// chunk's slot, and as (key, index, bits) composites at nbuf + base of the segment's
+// shared-memory buffer when to_smem.
+template <bool STRICT, bool BIG>
+__device__ __forceinline__ void write_flagged(const TopkParams& p, const StageInfo& si,
+                                              const uint8_t* buf, uint32_t flags, __half2 v2,
+                                              bool take_all, uint32_t base, Scratch<BIG>& sm,
+                                              uint32_t nbuf, bool to_smem) {
   const int tid = threadIdx.x;
-  const uint32_t vb = key_to_bits(kuse);
+  uint32_t* out = p.cand + si.slot * p.cap + base;
+  const long long e0 = si.cv0 * 8;
+  const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf);
+  uint32_t r = 0;
+  while (flags) {
+    const int j = __ffs(flags) - 1;
+    flags &= flags - 1;
+    const int vi = tid * kVecPerThread + j;
+    uint32_t m = vec_mask<STRICT>(si, buf, vi, v2, take_all);
+    while (m) {
+      const int e = __ffs(m) - 1;
+      m &= m - 1;
+      const uint32_t lidx = static_cast<uint32_t>(vi * 8 + e);
+      const uint32_t w = (static_cast<uint32_t>(v16[lidx]) << 16) | lidx;
+      out[r] = w;
+      if (to_smem) sm.cache[nbuf + base + r] = make_composite(w, e0, si.a0);
+      ++r;
+    }
+  }
+}
+
+// k-th smallest key among the n composites of the segment buffer, searched in [0, hi]
+// (kFewerThanK when fewer than k of them have key <= hi: then every candidate qualifies).  Each warp computes it independently (no barrier).
+template <bool BIG>
+__device__ __forceinline__ uint32_t buffer_kth_key(const Scratch<BIG>& sm, uint32_t n, uint32_t k,
+                                                   uint32_t hi) {
+  if (n < k) return kFewerThanK;
+  const int lane = threadIdx.x & 31;
+  {
+    uint32_t cnt = 0;
+    for (uint32_t i = lane; i < n; i += 32) cnt += static_cast<uint32_t>(sm.cache[i] >> 48) <= hi;
+    if (__reduce_add_sync(0xFFFFFFFFu, cnt) < k) return kFewerThanK;
+  }
+  uint32_t lo = 0;
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi) >> 1;
+    uint32_t cnt = 0;
+    for (uint32_t i = lane; i < n; i += 32) {
+      cnt += static_cast<uint32_t>(sm.cache[i] >> 48) <= mid ? 1u : 0u;
+    }
+    if (__reduce_add_sync(0xFFFFFFFFu, cnt) >= k) hi = mid; else lo = mid + 1;
+  }
+  return lo;
+}
+
+// Exact top-k selection among the chunk's candidates under threshold K (strict or not, or
+// take-all): the reference's two 8-bit digit passes plus ordered tie ranks.  Returns the
+// cutoff key; *S gets this thread's selected elements (bit 8*j+e), *sbase their first output
+// position and *stot the block total (== k).  Rare path.
+template <class SM>
+__device__ uint32_t exact_local_select(const TopkParams& p, const StageInfo& si,
+                                       const uint8_t* buf, SM& sm, uint32_t K, bool strict,
+                                       uint64_t* S_out, uint32_t* sbase_out, uint32_t* stot_out) {
+  const int tid = threadIdx.x;
+  const bool take_all = K == kNoThreshold;
+  const uint32_t vb = key_to_bits(K);
   const __half2 v2 = u32_as_h2(vb | (vb << 16));
-  const bool take_all = kuse == kNoThreshold;
-  const int sw = tid & 7;
   uint64_t M = 0;
-#pragma unroll
-  for (int jj = 0; jj < kVecPerThread; ++jj) {
-    const int j = jj ^ sw;  // rotate the read order: conflict-free 16-byte smem reads
+  for (int j = 0; j < kVecPerThread; ++j) {
     const int vi = tid * kVecPerThread + j;
     if (vi < si.nvc) {
-      const uint4 w = lds128(buf + vi * 16);
-      uint32_t m = take_all ? 0xFFu : ge_mask8(w, v2);
-      const long long gv = si.cv0 + vi;
-      if (gv * 8 < si.a0 || gv * 8 + 8 > si.a1) m &= valid_mask8(gv, si.a0, si.a1);
+      const uint32_t m = strict ? vec_mask<true>(si, buf, vi, v2, take_all)
+                                : vec_mask<false>(si, buf, vi, v2, take_all);
       M |= static_cast<uint64_t>(m) << (8 * j);
     }
   }
-  return M;
-}
-
-__device__ __forceinline__ void write_candidates(const TopkParams& p, const StageInfo& si,
-                                                 const uint8_t* buf, uint64_t M,
-                                                 uint32_t base) {
-  const int tid = threadIdx.x;
-  const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf) + tid * 64;
-  uint32_t* out = p.cand + si.slot * p.cap + base;
-  uint32_t r = 0;
-  while (M) {
-    const int pos = __ffsll(static_cast<long long>(M)) - 1;
-    M &= M - 1;
-    out[r++] = (static_cast<uint32_t>(v16[pos]) << 16) | static_cast<uint32_t>(tid * 64 + pos);
-  }
-}
-
-// Exact top-k of the chunk's candidates (more than cap of them survived the threshold).
-__device__ void exact_local(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
-                            ChunkSmem& sm, uint64_t M) {
-  const int tid = threadIdx.x;
   const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf) + tid * 64;
   RunHist rh;
-  for (uint64_t m = M; m; m &= m - 1) rh.add(sm.hist1, desc_key(v16[__ffsll(static_cast<long long>(m)) - 1]) >> 8);
+  for (uint64_t m = M; m; m &= m - 1) {
+    rh.add(sm.hist1, desc_key(v16[__ffsll(static_cast<long long>(m)) - 1]) >> 8);
+  }
   rh.flush(sm.hist1);
-  __syncthreads();
+  csync();
   if (tid < 32) warp_find_bin(sm.hist1, 0, p.k, &sm.bin1, &sm.before1);
-  __syncthreads();
+  csync();
   const uint32_t b1 = static_cast<uint32_t>(sm.bin1);
   for (uint64_t m = M; m; m &= m - 1) {
     const uint32_t key = desc_key(v16[__ffsll(static_cast<long long>(m)) - 1]);
     if ((key >> 8) == b1) rh.add(sm.hist2, key & 0xFFu);
   }
   rh.flush(sm.hist2);
-  __syncthreads();
+  csync();
   if (tid < 32) warp_find_bin(sm.hist2, sm.before1, p.k, &sm.bin2, &sm.before2);
-  __syncthreads();
+  csync();
   const uint32_t kstar = (b1 << 8) | static_cast<uint32_t>(sm.bin2);
   const uint32_t need = static_cast<uint32_t>(p.k) - sm.before2;
   uint32_t tcnt = 0;
@@ -298,7 +554,7 @@ __device__ void exact_local(const TopkParams& p, const StageInfo& si, const uint
     tcnt += desc_key(v16[__ffsll(static_cast<long long>(m)) - 1]) == kstar ? 1u : 0u;
   }
   uint32_t ttot;
-  const uint32_t tbase = block_excl_scan<kThreads>(tcnt, &ttot, sm.warp_tot);
+  const uint32_t tbase = block_excl_scan<kThreads, true>(tcnt, &ttot, sm.warp_tot);
   uint64_t S = 0;
   uint32_t tr = tbase;
   for (uint64_t m = M; m; m &= m - 1) {
@@ -311,278 +567,270 @@ __device__ void exact_local(const TopkParams& p, const StageInfo& si, const uint
       ++tr;
     }
   }
-  uint32_t stot;
-  const uint32_t sbase = block_excl_scan<kThreads>(static_cast<uint32_t>(__popcll(S)), &stot,
-                                                   sm.warp_tot);
-  write_candidates(p, si, buf, S, sbase);
-  if (tid == 0) {
-    p.chunk_count[si.slot] = stot;
-    if (p.stats) atomicAdd(&p.status[1], 1u);
-  }
+  *sbase_out =
+      block_excl_scan<kThreads, true>(static_cast<uint32_t>(__popcll(S)), stot_out, sm.warp_tot);
+  *S_out = S;
+  if (tid == 0 && p.stats) atomicAdd(&p.status[1], 1u);
   sm.hist1[tid] = 0;
   sm.hist2[tid] = 0;
+  return kstar;
 }
 
-__device__ void process_chunk(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
-                              ChunkSmem& sm) {
-  uint32_t kuse = si.g_prev;
-  bool selected = false;
-  if (kuse == kNoThreshold || !p.reuse) {
-    const uint32_t kc = chunk_select(p, si, buf, sm);
-    kuse = kc < kuse ? kc : kuse;
-    selected = true;
-  }
-  for (;;) {
-    const uint64_t M = candidate_mask(si, buf, kuse);
-    uint32_t total;
-    const uint32_t base = block_excl_scan<kThreads>(static_cast<uint32_t>(__popcll(M)), &total,
-                                                    sm.warp_tot);
-    if (total <= static_cast<uint32_t>(p.cap)) {
-      write_candidates(p, si, buf, M, base);
-      if (threadIdx.x == 0) {
-        p.chunk_count[si.slot] = total;
-        if (p.stats && !selected) atomicAdd(&p.status[2], 1u);
-      }
-      return;
-    }
-    if (!selected) {
-      const uint32_t kc = chunk_select(p, si, buf, sm);
-      kuse = kc < kuse ? kc : kuse;
-      selected = true;
-      continue;
-    }
-    exact_local(p, si, buf, sm, M);
-    return;
-  }
-}
-
-__global__ void __launch_bounds__(kThreads, 2)
-chunk_kernel(TopkParams p, long long total_work) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t* stages = smem;
-  ChunkSmem& sm = *reinterpret_cast<ChunkSmem*>(smem + kSmemOffScratch);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemOffBars);
-  StageInfo* info = reinterpret_cast<StageInfo*>(smem + kSmemOffInfo);
+// Large-k path: exact local select, written to the chunk's global slot and the segment's
+// shared-memory buffer.
+template <bool BIG>
+__device__ uint32_t exact_local(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
+                                Scratch<BIG>& sm, SegState& ss) {
   const int tid = threadIdx.x;
-
-  long long total = total_work;
-  if (p.offsets) {
-    const long long t = static_cast<long long>(p.chunk_start[p.seg_num]);
-    total = t < p.slot_capacity ? t : p.slot_capacity;
+  uint64_t S;
+  uint32_t sbase, stot;
+  const uint32_t kstar = exact_local_select(p, si, buf, sm, ss.K, ss.strict, &S, &sbase, &stot);
+  const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf) + tid * 64;
+  const bool to_smem = !ss.spilled && ss.nbuf + stot <= static_cast<uint32_t>(Cfg<BIG>::kCacheCap);
+  uint32_t* out = p.cand + si.slot * p.cap + sbase;
+  const long long e0 = si.cv0 * 8;
+  uint32_t r = 0;
+  for (uint64_t m = S; m; m &= m - 1) {
+    const int pos = __ffsll(static_cast<long long>(m)) - 1;
+    const uint32_t lidx = static_cast<uint32_t>(tid * 64 + pos);
+    const uint32_t w = (static_cast<uint32_t>(v16[pos]) << 16) | lidx;
+    out[r] = w;
+    if (to_smem) sm.cache[ss.nbuf + sbase + r] = make_composite(w, e0, si.a0);
+    ++r;
   }
-  if (tid == 0) {
-    for (int st = 0; st < kStages; ++st) mbar_init(&bars[st], 1);
-    fence_mbar_init();
-  }
-  sm.hist1[tid] = 0;
-  sm.hist2[tid] = 0;
-  __syncthreads();
-  const uint64_t policy = policy_evict_first();
-  if (tid == 0) {
-    for (int st = 0; st < kStages; ++st) {
-      const long long q = blockIdx.x + static_cast<long long>(st) * gridDim.x;
-      if (q < total) issue_chunk(p, q, &info[st], stages + st * kStageBytes, &bars[st], policy);
-    }
-  }
-  for (long long i = 0;; ++i) {
-    const long long q = blockIdx.x + i * gridDim.x;
-    if (q >= total) break;
-    const int st = static_cast<int>(i % kStages);
-    const uint32_t parity = static_cast<uint32_t>((i / kStages) & 1);
-    const bool ok = mbar_wait(&bars[st], parity);
-    if (__syncthreads_or(!ok)) {
-      // A bulk copy never completed: flag it, give in-flight copies one more bounded wait so
-      // no copy lands after this block's shared memory is released, and stop.
-      if (tid == 0) {
-        atomicOr(&p.status[0], kStatusWaitTimeout);
-        for (long long r = i; r < i + kStages; ++r) {
-          const long long qq = blockIdx.x + r * gridDim.x;
-          if (qq >= total) break;
-          mbar_wait(&bars[r % kStages], static_cast<uint32_t>((r / kStages) & 1));
-        }
-      }
-      __syncthreads();
-      return;
-    }
-    const StageInfo si = info[st];
-    if (si.nvc > 0) process_chunk(p, si, stages + st * kStageBytes, sm);
-    __syncthreads();
-    if (tid == 0) {
-      const long long q2 = q + static_cast<long long>(kStages) * gridDim.x;
-      if (q2 < total) issue_chunk(p, q2, &info[st], stages + st * kStageBytes, &bars[st], policy);
-    }
-  }
+  if (to_smem) ss.nbuf += stot; else ss.spilled = true;
+  if (tid == 0) p.chunk_count[si.slot] = stot;
+  return kstar;
 }
 
-// ---- merge -----------------------------------------------------------------------------
+enum ChunkResult { kChunkDone = 0, kChunkOverflow = 1, kChunkFail = 2 };
 
-struct alignas(16) MergeSmem {
-  uint32_t hist1[256];  // first: 16-byte aligned for warp_find_bin's 128-bit loads
-  uint32_t hist2[256];
-  unsigned long long sel[kMaxK];
-  uint32_t coff[kMaxChunksPerSegment + 1];
-  uint32_t warp_tot[kMergeThreads / 32];
-  int bin1, bin2;
-  uint32_t before1, before2;
+// Counts the chunk's candidates under (ss.K, STRICT) with one barrier, then writes them in
+// index order.  `par` selects the double-buffered warp-count slots.
+template <bool STRICT, bool BIG>
+__device__ int stream_chunk(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
+                            Scratch<BIG>& sm, SegState& ss, int par) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const bool take_all = ss.K == kNoThreshold;
+  const uint32_t vb = key_to_bits(ss.K);
+  const __half2 v2 = u32_as_h2(vb | (vb << 16));
+  uint32_t cnt;
+  const uint32_t flags = thread_flags<STRICT>(si, buf, v2, take_all, &cnt);
+  uint32_t incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) sm.wcnt[par][warp] = incl;
+  csync();
+  if (sm.fail) return kChunkFail;
+  uint32_t total = 0, wpre = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const uint32_t t = sm.wcnt[par][w];
+    wpre += w < warp ? t : 0u;
+    total += t;
+  }
+  if (total == 0) {
+    if (tid == 0) {
+      p.chunk_count[si.slot] = 0;
+      if (p.stats) atomicAdd(&p.status[2], 1u);
+    }
+    return kChunkDone;
+  }
+  if (total > static_cast<uint32_t>(p.cap)) return kChunkOverflow;
+  const uint32_t base = wpre + incl - cnt;
+  const bool to_smem = !ss.spilled && ss.nbuf + total <= static_cast<uint32_t>(Cfg<BIG>::kCacheCap);
+  if (flags) write_flagged<STRICT, BIG>(p, si, buf, flags, v2, take_all, base, sm, ss.nbuf, to_smem);
+  if (tid == 0) p.chunk_count[si.slot] = total;
+  if (to_smem) {
+    ss.nbuf += total;
+    ss.added += total;
+  } else {
+    ss.spilled = true;
+  }
+  if (!take_all) {
+    // >= k values with key <= K are now written (certified by this segment's own select or
+    // exact pass, earlier in index order): later chunks only need key < K.  Once k more
+    // candidates have arrived, tighten K to the exact k-th best of the buffer.
+    ss.strict = true;
+    if (ss.added >= static_cast<uint32_t>(p.k) && !ss.spilled) {
+      csync();
+      const uint32_t kk = buffer_kth_key(sm, ss.nbuf, static_cast<uint32_t>(p.k), ss.K);
+      if (kk < ss.K) ss.K = kk;
+      ss.added = 0;
+    }
+  }
+  return kChunkDone;
+}
+
+// First chunk of a segment (or one after an uncertified chunk): select a threshold, stream,
+// and fall back to the exact local select when too many values pass.
+template <bool BIG>
+__device__ int first_chunk(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
+                           Scratch<BIG>& sm, SegState& ss, int par) {
+  const uint32_t kc = chunk_select(p, si, buf, sm);
+  if (kc < ss.K) {
+    ss.K = kc;
+    ss.strict = false;
+  }
+  int r = ss.strict ? stream_chunk<true, BIG>(p, si, buf, sm, ss, par)
+                    : stream_chunk<false, BIG>(p, si, buf, sm, ss, par);
+  if (r == kChunkOverflow) {
+    ss.K = exact_local(p, si, buf, sm, ss);
+    ss.strict = true;
+    ss.added = 0;
+    r = kChunkDone;
+  }
+  return r;
+}
+
+// ---- consumer: segment merge -----------------------------------------------------------
+
+// Candidate source for the merge: the shared-memory cache or the chunk lists in global
+// memory (very long segments, many candidates, or a segment split across blocks).
+struct CacheSrc {
+  const unsigned long long* cache;
+  __device__ __forceinline__ unsigned long long get(uint32_t i) const { return cache[i]; }
 };
-static_assert(offsetof(MergeSmem, hist2) % 16 == 0, "hist alignment");
 
-// Walks this thread's contiguous range of the segment's concatenated candidate lists.
-struct ItemCursor {
+struct GlobalSrc {
   const TopkParams* p;
-  const MergeSmem* sm;
-  long long slot0;
-  long long first_elem;  // aligned element index of chunk 0's first vector
-  long long a0;
+  const uint32_t* coff;  // P + 1 prefix entries (shared or global memory)
+  int P;
+  long long slot0, v0, a0;
   int chunk_vecs;
-  int nch;
-  uint32_t i0, i1;
-
-  template <typename F>
-  __device__ __forceinline__ void for_each(F&& f) const {
-    if (i0 >= i1) return;
-    int lo = 0, hi = nch;  // largest c with coff[c] <= i0
+  __device__ __forceinline__ unsigned long long get(uint32_t i) const {
+    int lo = 0, hi = P;  // largest c with coff[c] <= i
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
-      if (sm->coff[mid] <= i0) lo = mid; else hi = mid;
+      if (coff[mid] <= i) lo = mid; else hi = mid;
     }
-    int c = lo;
-    for (uint32_t i = i0; i < i1; ++i) {
-      while (sm->coff[c + 1] <= i) ++c;
-      const uint32_t w = __ldcg(&p->cand[(slot0 + c) * p->cap + (i - sm->coff[c])]);
-      const uint32_t raw = w >> 16;
-      const long long elem = first_elem + static_cast<long long>(c) * chunk_vecs * 8 + (w & 0xFFFFu);
-      f(desc_key(raw), raw, static_cast<uint32_t>(elem - a0));
-    }
+    const uint32_t w = __ldcg(&p->cand[(slot0 + lo) * p->cap + (i - coff[lo])]);
+    return make_composite(w, (v0 + static_cast<long long>(lo) * chunk_vecs) * 8, a0);
   }
 };
 
-__global__ void __launch_bounds__(kMergeThreads) merge_kernel(TopkParams p) {
-  __shared__ __align__(16) MergeSmem sm;
-  constexpr int T = kMergeThreads;
+// Each of the n candidates with key <= kf takes the output slot given by its rank in
+// (key, index) order among them; composites are distinct, so ranks are exact.  Every
+// candidate ranking below another one with key <= kf also has key <= kf.
+__device__ __forceinline__ void rank_emit(const TopkParams& p, const unsigned long long* items,
+                                          uint32_t n, uint32_t kf, int s, long long len) {
   const int tid = threadIdx.x;
-  sm.hist1[tid] = 0;
-  sm.hist2[tid] = 0;
-  __syncthreads();
   const uint32_t k = static_cast<uint32_t>(p.k);
-  for (int s = blockIdx.x; s < p.seg_num; s += gridDim.x) {
-    const SegGeom g = seg_geom(p, s);
-    const long long slot0 = p.offsets ? static_cast<long long>(p.chunk_start[s])
-                                      : static_cast<long long>(s) * p.p_max;
-    const int nch = g.nchunks;
-    const bool bad = nch > kMaxChunksPerSegment ||
-                     (p.offsets && (slot0 + nch > p.slot_capacity ||
-                                    static_cast<long long>(p.chunk_start[s + 1]) - slot0 != nch));
-    uint16_t* ov = p.out_values + static_cast<long long>(s) * k;
-    int* oi = p.out_indices + static_cast<long long>(s) * k;
-    if (bad) {
-      if (tid == 0) {
-        atomicOr(&p.status[0], nch > kMaxChunksPerSegment ? kStatusSegmentTooLong : kStatusBadOffsets);
-      }
-      for (uint32_t r = tid; r < k; r += T) {
-        ov[r] = 0xFC00u;
-        oi[r] = -1;
-      }
-      continue;
+  uint16_t* ov = p.out_values + static_cast<long long>(s) * k;
+  int* oi = p.out_indices + static_cast<long long>(s) * k;
+  for (uint32_t e = tid; e < n; e += kThreads) {
+    const unsigned long long c = items[e];
+    if (static_cast<uint32_t>(c >> 48) > kf) continue;
+    uint32_t rank = 0;
+    for (uint32_t j = 0; j < n; ++j) rank += items[j] < c ? 1u : 0u;
+    if (rank < k) {
+      ov[rank] = static_cast<uint16_t>(c & 0xFFFFu);
+      oi[rank] = static_cast<int>((c >> 16) & 0xFFFFFFFFu);
     }
-    // prefix of the per-chunk candidate counts
-    const int per = (nch + T - 1) / T;
-    const int c0 = tid * per < nch ? tid * per : nch;
-    const int c1 = c0 + per < nch ? c0 + per : nch;
-    uint32_t local = 0;
-    for (int c = c0; c < c1; ++c) {
-      const uint32_t n = __ldcg(&p.chunk_count[slot0 + c]);
-      local += n < static_cast<uint32_t>(p.cap) ? n : static_cast<uint32_t>(p.cap);
+  }
+  // A segment shorter than k never certifies a threshold, so all n candidates are its
+  // values; the rest of the row is padding.
+  if (len < static_cast<long long>(k)) {
+    for (uint32_t r = n + tid; r < k; r += kThreads) {
+      ov[r] = 0xFC00u;
+      oi[r] = -1;
     }
-    uint32_t n_all;
-    uint32_t run = block_excl_scan<T>(local, &n_all, sm.warp_tot);
-    for (int c = c0; c < c1; ++c) {
-      sm.coff[c] = run;
-      const uint32_t n = __ldcg(&p.chunk_count[slot0 + c]);
-      run += n < static_cast<uint32_t>(p.cap) ? n : static_cast<uint32_t>(p.cap);
-    }
-    if (tid == 0) sm.coff[nch] = n_all;
-    __syncthreads();
-    const uint32_t kf = __ldcg(&p.seg_thresh[s]);
-    ItemCursor cur;
-    cur.p = &p;
-    cur.sm = &sm;
-    cur.slot0 = slot0;
-    cur.first_elem = g.v0 * 8;
-    cur.a0 = g.a0;
-    cur.chunk_vecs = g.chunk_vecs;
-    cur.nch = nch;
-    const uint32_t R = (n_all + T - 1) / T;
-    cur.i0 = tid * R < n_all ? tid * R : n_all;
-    cur.i1 = cur.i0 + R < n_all ? cur.i0 + R : n_all;
+  }
+  if (tid == 0 && p.stats) atomicAdd(&p.status[4], 1u);
+}
 
-    // exact cutoff over candidates with key <= kf: two 8-bit digit passes
-    RunHist rh;
-    cur.for_each([&](uint32_t key, uint32_t, uint32_t) {
-      if (key <= kf) rh.add(sm.hist1, key >> 8);
-    });
-    rh.flush(sm.hist1);
-    __syncthreads();
-    if (tid < 32) warp_find_bin(sm.hist1, 0, k, &sm.bin1, &sm.before1);
-    __syncthreads();
-    const int b1 = sm.bin1;
-    uint32_t kstar, need;
-    if (b1 >= 256) {  // fewer than k candidates (segment shorter than k): keep them all
-      kstar = 0x10000u;
-      need = 0;
-    } else {
-      cur.for_each([&](uint32_t key, uint32_t, uint32_t) {
-        if (key <= kf && (key >> 8) == static_cast<uint32_t>(b1)) rh.add(sm.hist2, key & 0xFFu);
-      });
-      rh.flush(sm.hist2);
-      __syncthreads();
-      if (tid < 32) warp_find_bin(sm.hist2, sm.before1, k, &sm.bin2, &sm.before2);
-      __syncthreads();
-      kstar = (static_cast<uint32_t>(b1) << 8) | static_cast<uint32_t>(sm.bin2);
-      need = k - sm.before2;
+// Exact top-k of the n candidates of `src` (index order) with key <= kf; writes row s.
+template <bool BIG, class Src>
+__device__ void select_and_emit(const TopkParams& p, const Src& src, uint32_t n, uint32_t kf,
+                                int s, long long seg_len, Scratch<BIG>& sm) {
+  const int tid = threadIdx.x;
+  const uint32_t k = static_cast<uint32_t>(p.k);
+  const uint32_t R = (n + kThreads - 1) / kThreads;
+  const uint32_t i0 = tid * R < n ? tid * R : n;
+  const uint32_t i1 = i0 + R < n ? i0 + R : n;
+  for (uint32_t j = 0; j < R; ++j) {
+    const uint32_t i = i0 + j;
+    uint32_t key = 0xFFFFFFFFu;
+    if (i < i1) key = static_cast<uint32_t>(src.get(i) >> 48);
+    hist_add_match(sm.hist1, key >> 8, key <= kf);
+  }
+  csync();
+  if (tid < 32) warp_find_bin(sm.hist1, 0, k, &sm.bin1, &sm.before1);
+  csync();
+  const int b1 = sm.bin1;
+  uint32_t kstar, need;
+  if (b1 >= 256) {  // fewer than k candidates (a segment shorter than k): keep them all
+    kstar = 0x10000u;
+    need = 0;
+  } else {
+    for (uint32_t j = 0; j < R; ++j) {
+      const uint32_t i = i0 + j;
+      uint32_t key = 0xFFFFFFFFu;
+      if (i < i1) key = static_cast<uint32_t>(src.get(i) >> 48);
+      hist_add_match(sm.hist2, key & 0xFFu, key <= kf && (key >> 8) == static_cast<uint32_t>(b1));
     }
-    // ties at the cutoff: ordered ranks
-    uint32_t tcnt = 0;
-    cur.for_each([&](uint32_t key, uint32_t, uint32_t) { tcnt += (key <= kf && key == kstar); });
-    uint32_t ttot;
-    const uint32_t tbase = block_excl_scan<T>(tcnt, &ttot, sm.warp_tot);
-    uint32_t scnt = 0;
-    {
-      uint32_t tr = tbase;
-      cur.for_each([&](uint32_t key, uint32_t, uint32_t) {
-        if (key > kf) return;
-        if (key < kstar) {
-          ++scnt;
-        } else if (key == kstar) {
-          scnt += tr < need;
-          ++tr;
-        }
-      });
+    csync();
+    if (tid < 32) warp_find_bin(sm.hist2, sm.before1, k, &sm.bin2, &sm.before2);
+    csync();
+    kstar = (static_cast<uint32_t>(b1) << 8) | static_cast<uint32_t>(sm.bin2);
+    need = k - sm.before2;
+  }
+  // ordered ranks of the ties at the cutoff
+  uint32_t tcnt = 0;
+  for (uint32_t i = i0; i < i1; ++i) {
+    const uint32_t key = static_cast<uint32_t>(src.get(i) >> 48);
+    tcnt += (key <= kf && key == kstar) ? 1u : 0u;
+  }
+  uint32_t ttot;
+  const uint32_t tbase = block_excl_scan<kThreads, true>(tcnt, &ttot, sm.warp_tot);
+  uint32_t scnt = 0;
+  {
+    uint32_t tr = tbase;
+    for (uint32_t i = i0; i < i1; ++i) {
+      const uint32_t key = static_cast<uint32_t>(src.get(i) >> 48);
+      if (key > kf) continue;
+      if (key < kstar) {
+        ++scnt;
+      } else if (key == kstar) {
+        scnt += tr < need ? 1u : 0u;
+        ++tr;
+      }
     }
-    uint32_t nsel;
-    const uint32_t sbase = block_excl_scan<T>(scnt, &nsel, sm.warp_tot);
-    {
-      uint32_t tr = tbase, w = sbase;
-      cur.for_each([&](uint32_t key, uint32_t raw, uint32_t idx) {
-        if (key > kf) return;
-        bool take = key < kstar;
-        if (key == kstar) {
-          take = tr < need;
-          ++tr;
-        }
-        if (take) {
-          sm.sel[w++] = (static_cast<unsigned long long>(key) << 48) |
-                        (static_cast<unsigned long long>(idx) << 16) | raw;
-        }
-      });
+  }
+  uint32_t nsel;
+  const uint32_t sbase = block_excl_scan<kThreads, true>(scnt, &nsel, sm.warp_tot);
+  {
+    uint32_t tr = tbase, w = sbase;
+    for (uint32_t i = i0; i < i1; ++i) {
+      const unsigned long long c = src.get(i);
+      const uint32_t key = static_cast<uint32_t>(c >> 48);
+      if (key > kf) continue;
+      bool take = key < kstar;
+      if (key == kstar) {
+        take = tr < need;
+        ++tr;
+      }
+      if (take) sm.sel[w++] = c;
     }
+  }
+  csync();
+  uint16_t* ov = p.out_values + static_cast<long long>(s) * k;
+  int* oi = p.out_indices + static_cast<long long>(s) * k;
+  if (nsel <= static_cast<uint32_t>(kThreads)) {
+    rank_emit(p, sm.sel, nsel, 0xFFFFu, s, 0);
+  } else {
     int n2 = 1;
     while (n2 < static_cast<int>(nsel)) n2 <<= 1;
-    for (int i = static_cast<int>(nsel) + tid; i < n2; i += T) sm.sel[i] = ~0ull;
-    __syncthreads();
+    for (int i = static_cast<int>(nsel) + tid; i < n2; i += kThreads) sm.sel[i] = ~0ull;
+    csync();
     for (int size = 2; size <= n2; size <<= 1) {
       for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        for (int i = tid; i < n2 / 2; i += T) {
+        for (int i = tid; i < n2 / 2; i += kThreads) {
           const int lo = 2 * i - (i & (stride - 1));
           const int hi = lo + stride;
           const bool up = (lo & size) == 0;
@@ -592,41 +840,264 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(TopkParams p) {
             sm.sel[hi] = a;
           }
         }
-        __syncthreads();
+        csync();
       }
     }
-    for (uint32_t r = tid; r < k; r += T) {
-      if (r < nsel) {
-        const unsigned long long c = sm.sel[r];
-        ov[r] = static_cast<uint16_t>(c & 0xFFFFu);
-        oi[r] = static_cast<int>((c >> 16) & 0xFFFFFFFFu);
-      } else {
-        ov[r] = 0xFC00u;
-        oi[r] = -1;
+    for (uint32_t r = tid; r < nsel; r += kThreads) {
+      const unsigned long long c = sm.sel[r];
+      ov[r] = static_cast<uint16_t>(c & 0xFFFFu);
+      oi[r] = static_cast<int>((c >> 16) & 0xFFFFFFFFu);
+    }
+    if (tid == 0 && p.stats) atomicAdd(&p.status[4], 1u);
+  }
+  for (uint32_t r = nsel + tid; r < k; r += kThreads) {
+    ov[r] = 0xFC00u;
+    oi[r] = -1;
+  }
+  if (tid == 0 && nsel < k && seg_len >= static_cast<long long>(k)) {
+    atomicOr(&p.status[0], kStatusCertifyFailed);
+  }
+  sm.hist1[tid] = 0;
+  sm.hist2[tid] = 0;
+  csync();
+}
+
+// Emits row s from the n candidates in sm.cache (key <= kf qualifies).
+template <bool BIG>
+__device__ __forceinline__ void emit_from_cache(const TopkParams& p, Scratch<BIG>& sm, uint32_t n,
+                                                uint32_t kf, int s, long long len) {
+  const uint32_t k = static_cast<uint32_t>(p.k);
+  if (!BIG) {
+    const uint32_t kk = buffer_kth_key(sm, n, k, kf);  // exact cutoff key of the row
+    if (kk == kFewerThanK && len >= static_cast<long long>(k) && threadIdx.x == 0) {
+      atomicOr(&p.status[0], kStatusCertifyFailed);  // fewer than k candidates survived
+    }
+    rank_emit(p, sm.cache, n, kk, s, len);
+  } else {
+    CacheSrc cs{sm.cache};
+    select_and_emit<BIG>(p, cs, n, kf, s, len, sm);
+  }
+}
+
+// Merges segment ss.s from the chunk lists in global memory (split or overflowing segments).
+template <bool BIG>
+__device__ void merge_from_global(const TopkParams& p, const SegState& ss, uint32_t kf,
+                                  Scratch<BIG>& sm) {
+  using C = Cfg<BIG>;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int P = ss.nchunks;
+  const bool small_p = P <= C::kCoffCap;
+  uint32_t* coff = small_p ? sm.coff : p.chunk_off + ss.slot0;
+  if (tid < 32) {  // prefix of the per-chunk candidate counts
+    uint32_t carry = 0;
+    for (int base = 0; base < P; base += 32) {
+      const int c = base + lane;
+      uint32_t n = 0;
+      if (c < P) {
+        n = __ldcg(&p.chunk_count[ss.slot0 + c]);
+        n = n < static_cast<uint32_t>(p.cap) ? n : static_cast<uint32_t>(p.cap);
+      }
+      uint32_t incl = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (c < P) coff[c] = carry + incl - n;
+      carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
+    }
+    if (lane == 0) {
+      coff[P] = carry;
+      sm.bcast[2] = carry;
+    }
+  }
+  if (!small_p) __threadfence_block();
+  csync();
+  const uint32_t n = sm.bcast[2];
+  const long long len = ss.a1 - ss.a0;
+  if (small_p && n <= static_cast<uint32_t>(C::kCacheCap)) {
+    const int warp = tid >> 5;
+    for (int c = warp; c < P; c += kWarps) {
+      const uint32_t o = sm.coff[c];
+      const uint32_t cnt = sm.coff[c + 1] - o;
+      const uint32_t* src = p.cand + (ss.slot0 + c) * p.cap;
+      const long long e0 = (ss.v0 + static_cast<long long>(c) * ss.chunk_vecs) * 8;
+      for (uint32_t i = lane; i < cnt; i += 32) {
+        sm.cache[o + i] = make_composite(__ldcg(src + i), e0, ss.a0);
       }
     }
-    if (tid == 0) {
-      if (nsel < k && g.a1 - g.a0 >= static_cast<long long>(k)) atomicOr(&p.status[0], kStatusCertifyFailed);
-      if (p.stats) atomicAdd(&p.status[4], 1u);
+    csync();
+    emit_from_cache<BIG>(p, sm, n, kf, ss.s, len);
+  } else {
+    GlobalSrc gs{&p, coff, P, ss.slot0, ss.v0, ss.a0, ss.chunk_vecs};
+    select_and_emit<BIG>(p, gs, n, kf, ss.s, len, sm);
+  }
+}
+
+// The CTA has finished its chunks of segment ss.s: merge it here if no other CTA still
+// holds some of them.
+template <bool BIG>
+__device__ void close_segment(const TopkParams& p, const SegState& ss, Scratch<BIG>& sm) {
+  if (ss.mycnt == 0) return;
+  uint32_t kf = ss.K;
+  const bool split = ss.mycnt != ss.nchunks;
+  if (split) {
+    __threadfence();  // this thread's candidate writes, before the arrival below
+    csync();
+    if (threadIdx.x == 0) {
+      if (ss.K < kNoThreshold) atomicMin(&p.seg_thresh[ss.s], ss.K);
+      __threadfence();
+      const uint32_t old = atomicAdd(&p.seg_done[ss.s], static_cast<uint32_t>(ss.mycnt));
+      const bool last = old + static_cast<uint32_t>(ss.mycnt) == static_cast<uint32_t>(ss.nchunks);
+      uint32_t k2 = ss.K;
+      if (last) {
+        __threadfence();
+        const uint32_t g = __ldcg(&p.seg_thresh[ss.s]);
+        k2 = g < k2 ? g : k2;
+      }
+      sm.bcast[0] = last ? 1u : 0u;
+      sm.bcast[1] = k2;
     }
+    csync();
+    if (!sm.bcast[0]) return;
+    kf = sm.bcast[1];
+    __threadfence();
+  }
+  csync();  // every consumer's candidate writes for this segment are done
+  if (!split && !ss.spilled) {
+    emit_from_cache<BIG>(p, sm, ss.nbuf, kf, ss.s, ss.a1 - ss.a0);
+    return;
+  }
+  merge_from_global<BIG>(p, ss, kf, sm);
+}
+
+template <bool BIG>
+__device__ void consumer_loop(const TopkParams& p, long long q0, long long q1, uint8_t* stages,
+                              uint64_t* full, uint64_t* empty, const StageInfo* info,
+                              Scratch<BIG>& sm) {
+  constexpr int S = Cfg<BIG>::kStagesN;
+  SegState ss;
+  long long i = 0;
+  for (long long q = q0; q < q1; ++q, ++i) {
+    const int st = static_cast<int>(i % S);
+    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>((i / S) & 1));
+    if (!ok) sm.fail = 1u;
+    const StageInfo& si = info[st];  // read in place: valid until this stage is released
+    const uint8_t* buf = stages + static_cast<size_t>(st) * kStageBytes;
+    const int par = static_cast<int>(i & 1);
+    int r = kChunkDone;
+    if (si.s == ss.s && ss.strict && si.nvc > 0) {
+      // steady state: one barrier per chunk, usually nothing to write
+      r = stream_chunk<true, BIG>(p, si, buf, sm, ss, par);
+      if (r == kChunkOverflow) r = first_chunk<BIG>(p, si, buf, sm, ss, par);  // values ramped up
+    } else {
+      if (group_or<kThreads>(!ok)) r = kChunkFail;
+      if (r != kChunkFail) {
+        if (si.s != ss.s) {
+          close_segment<BIG>(p, ss, sm);
+          ss = SegState{};
+          ss.s = si.s;
+          ss.nchunks = si.nchunks;
+          ss.chunk_vecs = si.chunk_vecs;
+          ss.slot0 = si.slot - si.c;
+          ss.v0 = si.v0;
+          ss.a0 = si.a0;
+          ss.a1 = si.a1;
+        }
+        if (si.nvc > 0) r = first_chunk<BIG>(p, si, buf, sm, ss, par);
+      }
+    }
+    if (r == kChunkFail) {  // a bulk copy never arrived: stop (the stage contents are not valid)
+      if (threadIdx.x == 0) atomicOr(&p.status[0], kStatusWaitTimeout);
+      return;
+    }
+    if (si.nvc > 0) ++ss.mycnt;
+    release_stage(&empty[st]);
+  }
+  close_segment<BIG>(p, ss, sm);
+}
+
+}  // namespace bt
+
+#include "bt_small.cuh"
+
+namespace bt {
+
+// 96 registers: each SM sub-partition (16K registers) holds 5 warps, so two 9-warp blocks fit.
+template <bool BIG>
+__global__ void __maxnreg__(96)
+topk_kernel(TopkParams p, long long work_total) {
+  using L = SmemLayout<BIG>;
+  constexpr int S = L::S;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* stages = smem;
+  Scratch<BIG>& sm = *reinterpret_cast<Scratch<BIG>*>(smem + L::off_scratch);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::off_full);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L::off_empty);
+  StageInfo* info = reinterpret_cast<StageInfo*>(smem + L::off_info);
+  const int tid = threadIdx.x;
+
+  long long W = work_total;
+  if (p.offsets) {
+    const long long t = static_cast<long long>(p.chunk_start[p.seg_num]);
+    W = t < p.slot_capacity ? t : p.slot_capacity;
+  }
+  const long long q0 = W * blockIdx.x / gridDim.x;
+  const long long q1 = W * (blockIdx.x + 1) / gridDim.x;
+  if (tid == 0) {
+    if constexpr (!BIG) {
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&sm.batch_full[b], kWarps);
+        mbar_init(&sm.batch_free[b], 1);
+      }
+      sm.kpub = ~0ull;  // tagged with segment -1: matches nothing
+    }
+    for (int st = 0; st < S; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], kWarps);  // one arrival per consumer warp
+      StageInfo z{};
+      z.s = -1;
+      z.vlo = z.vhi = -1;
+      info[st] = z;  // a wait that times out then sees an empty item, never garbage
+    }
+    fence_mbar_init();
+    sm.fail = 0u;
+  }
+  if (tid < 256) {
     sm.hist1[tid] = 0;
     sm.hist2[tid] = 0;
-    __syncthreads();
+  }
+  __syncthreads();
+  if (tid >= kThreads) {
+    if (tid == kThreads) {
+      producer_loop<BIG>(p, q0, q1, stages, full, empty, info);
+    } else if (!BIG && tid >= kThreads + 32) {
+      if constexpr (!BIG) merger_loop(p, sm);
+    }
+    return;
+  }
+  if constexpr (BIG) {
+    consumer_loop<true>(p, q0, q1, stages, full, empty, info, sm);
+  } else {
+    consumer_loop_small(p, q0, q1, stages, full, empty, info, sm);
   }
 }
 
 // ---- set-up kernels -------------------------------------------------------------------
 
-// Fixed-length rows: reset the per-segment thresholds and the status words.
+// Fixed-length rows: reset the per-segment thresholds, arrival counters and status words.
 __global__ void init_kernel(TopkParams p) {
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (i < 16) p.status[i] = 0;
   for (long long s = i; s < p.seg_num; s += static_cast<long long>(gridDim.x) * blockDim.x) {
     p.seg_thresh[s] = kNoThreshold;
+    p.seg_done[s] = 0;
   }
 }
 
-// CSR batches: thresholds, status, and the chunk-slot prefix over segments (one block).
+// CSR batches: the same resets, the chunk-slot prefix over segments, and the padding rows of
+// empty segments (which no chunk work item covers).  One block.
 __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
   __shared__ uint32_t warp_tot[32];
   const int tid = threadIdx.x;
@@ -638,8 +1109,17 @@ __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
     uint32_t nch = 0;
     if (s < p.seg_num) {
       p.seg_thresh[s] = kNoThreshold;
+      p.seg_done[s] = 0;
       nch = static_cast<uint32_t>(seg_geom(p, s).nchunks);
-      if (p.offsets[s] < 0 || p.offsets[s + 1] < p.offsets[s]) atomicOr(&p.status[0], kStatusBadOffsets);
+      if (p.offsets[s] < 0 || p.offsets[s + 1] < p.offsets[s]) {
+        atomicOr(&p.status[0], kStatusBadOffsets);
+      }
+      if (nch == 0) {
+        for (int r = 0; r < p.k; ++r) {
+          p.out_values[static_cast<long long>(s) * p.k + r] = 0xFC00u;
+          p.out_indices[static_cast<long long>(s) * p.k + r] = -1;
+        }
+      }
     }
     uint32_t tot;
     const uint32_t pre = block_excl_scan<1024>(nch, &tot, warp_tot);

@@ -1,0 +1,479 @@
+// bt_small.cuh -- the k <= 128 pipeline: streaming consumers + a merger warp.
+//
+// Consumers (8 warps) test each chunk against the segment's threshold and hand the
+// survivors, as (key, index, bits) composites, to the merger through a double-buffered
+// shared-memory batch.  The merger warp keeps the exact running top-k of the segment (a
+// sorted list of <= k composites) and publishes its k-th key; consumers adopt it as a
+// strict threshold at their next chunk barrier (k candidates with that key or better, all
+// at lower indices, already exist).  At the segment's last chunk the list is the answer.
+// A segment shared by two blocks goes through global partial lists and an arrival counter;
+// the last block to arrive merges them.
+#pragma once
+
+
+namespace bt {
+
+// ---- consumer ----------------------------------------------------------------------------
+
+struct Counted {
+  uint32_t flags, cnt, base, total, knext;
+  bool fail;
+};
+
+// Counts this chunk's candidates under (K, STRICT) with one barrier and picks up the merger's
+// latest threshold for segment `seg` (uniform: staged through kuse[par] by thread 0).
+template <bool STRICT>
+__device__ __forceinline__ Counted count_chunk(const StageInfo& si, const uint8_t* buf,
+                                               SmallScratch& sm, uint32_t K, int par, int seg) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const bool take_all = K == kNoThreshold;
+  const uint32_t vb = key_to_bits(K);
+  const __half2 v2 = u32_as_h2(vb | (vb << 16));
+  Counted c;
+  c.flags = thread_flags<STRICT>(si, buf, v2, take_all, &c.cnt);
+  uint32_t incl = c.cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) sm.wcnt[par][warp] = incl;
+  if (tid == 0) {
+    const unsigned long long kp = *reinterpret_cast<volatile unsigned long long*>(&sm.kpub);
+    sm.kuse[par] = (static_cast<int>(kp >> 32) == seg) ? static_cast<uint32_t>(kp & 0xFFFFu)
+                                                       : kNoThreshold;
+  }
+  csync();
+  c.fail = sm.fail != 0;
+  uint32_t total = 0, wpre = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const uint32_t t = sm.wcnt[par][w];
+    wpre += w < warp ? t : 0u;
+    total += t;
+  }
+  c.total = total;
+  c.base = wpre + incl - c.cnt;
+  c.knext = sm.kuse[par];
+  return c;
+}
+
+// Writes this thread's flagged candidates as composites at batch[base ...].
+template <bool STRICT>
+__device__ __forceinline__ void write_batch(const StageInfo& si, const uint8_t* buf, uint32_t flags,
+                                            uint32_t K, uint32_t base, unsigned long long* batch) {
+  const int tid = threadIdx.x;
+  const bool take_all = K == kNoThreshold;
+  const uint32_t vb = key_to_bits(K);
+  const __half2 v2 = u32_as_h2(vb | (vb << 16));
+  const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf);
+  const long long e0 = si.cv0 * 8;
+  uint32_t r = 0;
+  while (flags) {
+    const int j = __ffs(flags) - 1;
+    flags &= flags - 1;
+    const int vi = tid * kVecPerThread + j;
+    uint32_t m = vec_mask<STRICT>(si, buf, vi, v2, take_all);
+    while (m) {
+      const int e = __ffs(m) - 1;
+      m &= m - 1;
+      const uint32_t lidx = static_cast<uint32_t>(vi * 8 + e);
+      batch[base + r++] =
+          make_composite((static_cast<uint32_t>(v16[lidx]) << 16) | lidx, e0, si.a0);
+    }
+  }
+}
+
+// Waits until batch buffer b may be overwritten (the merger released its previous use).
+__device__ __forceinline__ bool wait_batch_free(SmallScratch& sm, long long nb) {
+  if (nb < 2) return true;
+  return mbar_wait(&sm.batch_free[nb & 1], static_cast<uint32_t>(((nb >> 1) - 1) & 1));
+}
+
+__device__ __forceinline__ void send_batch(SmallScratch& sm, int b, const BatchMeta& meta) {
+  if (threadIdx.x == 0) sm.meta[b] = meta;
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.batch_full[b]);
+}
+
+// One non-empty chunk: threshold, count, write the batch, hand it to the merger.
+__device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
+                           SmallScratch& sm, SegState& ss, int par, long long nb,
+                           uint32_t* guess) {
+  const uint32_t k = static_cast<uint32_t>(p.k);
+  const uint32_t cap = static_cast<uint32_t>(p.cap);
+  uint32_t K = ss.K;
+  bool strict = ss.strict;
+  Counted c;
+  if (strict) {
+    c = count_chunk<true>(si, buf, sm, K, par, ss.s);
+  } else {
+    bool have = false;
+    if (ss.mycnt == 0 && *guess != kNoThreshold) {
+      // the previous segment's first-chunk threshold, verified on this chunk: accepted when
+      // it leaves between k and cap candidates here (then it is certified by this chunk)
+      c = count_chunk<false>(si, buf, sm, *guess, par, ss.s);
+      if (c.fail) return kChunkFail;
+      if (c.total >= k && c.total <= cap) {
+        K = *guess;
+        have = true;
+        if (threadIdx.x == 0 && p.stats) atomicAdd(&p.status[5], 1u);
+      }
+    }
+    if (!have) {
+      K = chunk_select(p, si, buf, sm);
+      if (ss.mycnt == 0) *guess = K;
+      c = count_chunk<false>(si, buf, sm, K, par, ss.s);
+    }
+    strict = false;
+  }
+  if (c.fail) return kChunkFail;
+  const int b = static_cast<int>(nb & 1);
+  uint32_t n = c.total;
+  bool written = false;
+  if (n > cap) {
+    // too many survivors (rising values): a tighter chunk threshold, else the exact select
+    if (strict) {
+      const uint32_t kc = chunk_select(p, si, buf, sm);
+      if (kc < K) {
+        const Counted c2 = count_chunk<false>(si, buf, sm, kc, par, ss.s);
+        if (c2.fail) return kChunkFail;
+        if (c2.total <= cap) {
+          K = kc;
+          strict = false;
+          c = c2;
+          n = c2.total;
+        }
+      }
+    }
+    if (n > cap) {
+      uint64_t S;
+      uint32_t sbase, stot;
+      const uint32_t kstar = exact_local_select(p, si, buf, sm, K, strict, &S, &sbase, &stot);
+      if (!wait_batch_free(sm, nb)) return kChunkFail;
+      const int tid = threadIdx.x;
+      const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf) + tid * 64;
+      const long long e0 = si.cv0 * 8;
+      uint32_t r = 0;
+      for (uint64_t m = S; m; m &= m - 1) {
+        const int pos = __ffsll(static_cast<long long>(m)) - 1;
+        const uint32_t lidx = static_cast<uint32_t>(tid * 64 + pos);
+        sm.batch[b][sbase + r++] =
+            make_composite((static_cast<uint32_t>(v16[pos]) << 16) | lidx, e0, si.a0);
+      }
+      K = kstar;
+      strict = true;
+      n = stot;
+      written = true;
+    }
+  }
+  if (!written) {
+    if (!wait_batch_free(sm, nb)) return kChunkFail;
+    if (c.flags) {
+      if (strict) write_batch<true>(si, buf, c.flags, K, c.base, sm.batch[b]);
+      else write_batch<false>(si, buf, c.flags, K, c.base, sm.batch[b]);
+    }
+  }
+  // >= k values with key <= K are in the batches now (this chunk certified K, or an earlier
+  // one did): later chunks of the segment only need key < K.
+  if (K != kNoThreshold) {
+    ss.K = K;
+    ss.strict = true;
+  }
+  if (c.knext < ss.K) {  // the merger's k-th key: k candidates at lower indices beat ties
+    ss.K = c.knext;
+    ss.strict = true;
+  }
+  BatchMeta meta;
+  meta.len = si.a1 - si.a0;
+  meta.part_slot = ss.slot0;
+  meta.seg_slot = si.slot - si.c;
+  meta.s = si.s;
+  meta.n = n;
+  meta.flags = si.last ? kBatchEnd : 0;
+  meta.mycnt = ss.mycnt + 1;
+  meta.nchunks = si.nchunks;
+  meta.K = ss.K;
+  send_batch(sm, b, meta);
+  if (threadIdx.x == 0 && p.stats && n == 0) atomicAdd(&p.status[2], 1u);
+  return kChunkDone;
+}
+
+__device__ void consumer_loop_small(const TopkParams& p, long long q0, long long q1,
+                                    uint8_t* stages, uint64_t* full, uint64_t* empty,
+                                    const StageInfo* info, SmallScratch& sm) {
+  constexpr int S = Cfg<false>::kStagesN;
+  SegState ss;
+  uint32_t guess = kNoThreshold;
+  long long nb = 0;  // batches sent
+  long long i = 0;
+  bool failed = false;
+  for (long long q = q0; q < q1; ++q, ++i) {
+    const int st = static_cast<int>(i % S);
+    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>((i / S) & 1));
+    if (!ok) sm.fail = 1u;
+    const StageInfo& si = info[st];  // read in place: valid until this stage is released
+    if (si.nvc == 0) {
+      release_stage(&empty[st]);
+      continue;
+    }
+    if (si.s != ss.s) {
+      ss = SegState{};
+      ss.s = si.s;
+      ss.slot0 = si.slot;  // first slot of this block's part of the segment
+    }
+    const int r = small_chunk(p, si, stages + static_cast<size_t>(st) * kStageBytes, sm, ss,
+                              static_cast<int>(i & 1), nb, &guess);
+    if (r == kChunkFail) {
+      failed = true;
+      break;
+    }
+    ++ss.mycnt;
+    ++nb;
+    release_stage(&empty[st]);
+  }
+  // tell the merger to stop (bounded wait for the buffer)
+  wait_batch_free(sm, nb);
+  csync();
+  if ((failed || sm.fail) && threadIdx.x == 0) atomicOr(&p.status[0], kStatusWaitTimeout);
+  BatchMeta stop{};
+  stop.flags = kBatchStop;
+  send_batch(sm, static_cast<int>(nb & 1), stop);
+}
+
+// ---- merger ----------------------------------------------------------------------------------
+//
+// The running top-k is held in registers: a sorted (ascending) sequence of N = 32*R 64-bit
+// composites, element r*32+lane in x[r] of lane `lane`.  A batch is loaded in the same layout,
+// sorted with a bitonic network, and merged in: C[i] = min(L[i], B[N-1-i]) holds the N
+// smallest of L and B as a bitonic sequence, and one bitonic merge pass sorts it.
+
+constexpr unsigned long long kEmpty = ~0ull;  // never a composite (indices are < 2^32 - 1)
+
+__device__ __forceinline__ unsigned long long shfl64(unsigned long long v, int src) {
+  const uint32_t lo = __shfl_sync(0xFFFFFFFFu, static_cast<uint32_t>(v), src);
+  const uint32_t hi = __shfl_sync(0xFFFFFFFFu, static_cast<uint32_t>(v >> 32), src);
+  return (static_cast<unsigned long long>(hi) << 32) | lo;
+}
+
+__device__ __forceinline__ unsigned long long shfl_xor64(unsigned long long v, int mask) {
+  const uint32_t lo = __shfl_xor_sync(0xFFFFFFFFu, static_cast<uint32_t>(v), mask);
+  const uint32_t hi = __shfl_xor_sync(0xFFFFFFFFu, static_cast<uint32_t>(v >> 32), mask);
+  return (static_cast<unsigned long long>(hi) << 32) | lo;
+}
+
+// One bitonic compare-exchange step (block `size`, distance `stride`) over the striped array;
+// size == 0 means "ascending everywhere" (the final merge of a bitonic sequence).
+template <int R>
+__device__ __forceinline__ void bitonic_step(unsigned long long (&x)[R], int size, int stride) {
+  const int lane = threadIdx.x & 31;
+  if (stride >= 32) {
+    const int rs = stride >> 5;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if ((r & rs) == 0) {
+        const bool up = size == 0 || (((r << 5) + lane) & size) == 0;
+        const unsigned long long a = x[r], b = x[r | rs];
+        if ((a > b) == up) {
+          x[r] = b;
+          x[r | rs] = a;
+        }
+      }
+    }
+  } else {
+    const bool lower = (lane & stride) == 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const bool up = size == 0 || (((r << 5) + lane) & size) == 0;
+      const unsigned long long y = shfl_xor64(x[r], stride);
+      const unsigned long long mn = x[r] < y ? x[r] : y;
+      const unsigned long long mx = x[r] < y ? y : x[r];
+      x[r] = (lower == up) ? mn : mx;
+    }
+  }
+}
+
+template <int R>
+__device__ __forceinline__ void warp_sort_regs(unsigned long long (&x)[R]) {
+#pragma unroll
+  for (int size = 2; size <= 32 * R; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) bitonic_step<R>(x, size, stride);
+  }
+}
+
+// L <- the N smallest of L and B, both ascending.
+template <int R>
+__device__ __forceinline__ void merge_sorted(unsigned long long (&L)[R], const unsigned long long (&B)[R]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const unsigned long long b = shfl64(B[R - 1 - r], 31 - lane);  // B[N-1-i]
+    L[r] = L[r] < b ? L[r] : b;
+  }
+#pragma unroll
+  for (int stride = 16 * R; stride > 0; stride >>= 1) bitonic_step<R>(L, 0, stride);
+}
+
+// Element i of the striped array (all lanes get it).
+template <int R>
+__device__ __forceinline__ unsigned long long element(const unsigned long long (&x)[R], int i) {
+  unsigned long long v = x[0];
+#pragma unroll
+  for (int r = 1; r < R; ++r) v = (i >> 5) == r ? x[r] : v;
+  return shfl64(v, i & 31);
+}
+
+// Merges m composites from `src` (shared or global memory; `sorted` when already ascending).
+template <int R>
+__device__ __forceinline__ void absorb(unsigned long long (&L)[R], const unsigned long long* src,
+                                       int m, bool sorted) {
+  const int lane = threadIdx.x & 31;
+  for (int base = 0; base < m; base += 32 * R) {
+    unsigned long long B[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int i = base + (r << 5) + lane;
+      B[r] = i < m ? src[i] : kEmpty;
+    }
+    if (!sorted) warp_sort_regs<R>(B);
+    merge_sorted<R>(L, B);
+  }
+}
+
+template <int R>
+__device__ __forceinline__ void emit_row(const TopkParams& p, int s, const unsigned long long (&L)[R],
+                                         int nl, long long len) {
+  const int lane = threadIdx.x & 31;
+  const int k = p.k;
+  uint16_t* ov = p.out_values + static_cast<long long>(s) * k;
+  int* oi = p.out_indices + static_cast<long long>(s) * k;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int pos = (r << 5) + lane;
+    if (pos < k) {
+      if (pos < nl) {
+        ov[pos] = static_cast<uint16_t>(L[r] & 0xFFFFu);
+        oi[pos] = static_cast<int>((L[r] >> 16) & 0xFFFFFFFFu);
+      } else {
+        ov[pos] = 0xFC00u;
+        oi[pos] = -1;
+      }
+    }
+  }
+  if (lane == 0) {
+    if (nl < k && len >= k) atomicOr(&p.status[0], kStatusCertifyFailed);
+    if (p.stats) atomicAdd(&p.status[4], 1u);
+  }
+}
+
+// End of this block's part of a segment: emit the row, or publish the partial list and, if
+// this block arrives last, merge all parts.
+template <int R>
+__device__ void finalize_part(const TopkParams& p, const BatchMeta& m, unsigned long long (&L)[R],
+                              int nl) {
+  const int lane = threadIdx.x & 31;
+  const int k = p.k;
+  if (m.mycnt == m.nchunks) {
+    emit_row<R>(p, m.s, L, nl, m.len);
+    return;
+  }
+  // partial list (its first min(nl, k) entries) -> the cand region of this part's first slot
+  const int np = nl < k ? nl : k;
+  unsigned long long* dst = reinterpret_cast<unsigned long long*>(p.cand + m.part_slot * p.cap);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int pos = (r << 5) + lane;
+    if (pos < np) dst[pos] = L[r];
+  }
+  for (int c = lane; c < m.mycnt; c += 32) {
+    p.chunk_count[m.part_slot + c] = c == 0 ? static_cast<uint32_t>(np) : 0u;
+  }
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    if (m.K < kNoThreshold) atomicMin(&p.seg_thresh[m.s], m.K);
+    __threadfence();
+    const uint32_t old = atomicAdd(&p.seg_done[m.s], static_cast<uint32_t>(m.mycnt));
+    last = old + static_cast<uint32_t>(m.mycnt) == static_cast<uint32_t>(m.nchunks);
+  }
+  last = __shfl_sync(0xFFFFFFFFu, last, 0);
+  if (!last) return;
+  __threadfence();
+  int n = nl;
+  for (int c = 0; c < m.nchunks; ++c) {
+    const long long slot = m.seg_slot + c;
+    if (slot == m.part_slot) continue;  // this block's own part is already in L
+    int cnt = static_cast<int>(__ldcg(&p.chunk_count[slot]));
+    if (cnt <= 0) continue;
+    cnt = cnt < k ? cnt : k;  // a partial list holds at most k entries, ascending
+    absorb<R>(L, reinterpret_cast<const unsigned long long*>(p.cand + slot * p.cap), cnt, true);
+    n += cnt;
+  }
+  emit_row<R>(p, m.s, L, n < 32 * R ? n : 32 * R, m.len);
+}
+
+template <int R>
+__device__ void merger_loop_r(const TopkParams& p, SmallScratch& sm) {
+  const int lane = threadIdx.x & 31;
+  const int k = p.k;
+  unsigned long long L[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) L[r] = kEmpty;
+  long long nbm = 0;
+  int cur = -1;
+  int nl = 0;
+  for (;;) {
+    const int b = static_cast<int>(nbm & 1);
+    if (!mbar_wait(&sm.batch_full[b], static_cast<uint32_t>((nbm >> 1) & 1))) {
+      if (lane == 0) atomicOr(&p.status[0], kStatusWaitTimeout);
+      return;
+    }
+    const BatchMeta m = sm.meta[b];
+    if (m.flags & kBatchStop) return;
+    if (m.s != cur) {
+      cur = m.s;
+      nl = 0;
+#pragma unroll
+      for (int r = 0; r < R; ++r) L[r] = kEmpty;
+    }
+    const int nb = static_cast<int>(m.n);
+    if (nb > 0) {
+      absorb<R>(L, sm.batch[b], nb, false);
+      nl = nl + nb < 32 * R ? nl + nb : 32 * R;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.batch_free[b]);
+    if (nb > 0 && nl >= k) {
+      const unsigned long long kth = element<R>(L, k - 1);
+      if (lane == 0) {
+        *reinterpret_cast<volatile unsigned long long*>(&sm.kpub) =
+            (static_cast<unsigned long long>(static_cast<uint32_t>(m.s)) << 32) |
+            static_cast<uint32_t>(kth >> 48);
+      }
+    }
+    if (m.flags & kBatchEnd) {
+      finalize_part<R>(p, m, L, nl);
+      cur = -1;
+      nl = 0;
+#pragma unroll
+      for (int r = 0; r < R; ++r) L[r] = kEmpty;
+    }
+    ++nbm;
+  }
+}
+
+__device__ void merger_loop(const TopkParams& p, SmallScratch& sm) {
+  if (p.k <= 32) {
+    merger_loop_r<1>(p, sm);
+  } else if (p.k <= 64) {
+    merger_loop_r<2>(p, sm);
+  } else {
+    merger_loop_r<4>(p, sm);
+  }
+}
+
+}  // namespace bt

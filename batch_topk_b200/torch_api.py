@@ -95,3 +95,38 @@ def topk_segmented(x: torch.Tensor, offsets: torch.Tensor, k: int, *,
     if rc != 0:
         raise BatchTopkError(rc, "bt_topk_half_segmented")
     return vals, idx
+
+
+_staging: dict = {}
+
+
+def topk_from_host(x_host: torch.Tensor, k: int, *, out_host: tuple | None = None,
+                   stream=None, workspace: Workspace | None = None, device=None):
+    """End-to-end call from host memory: copy the rows in, run top-k, copy the results out.
+
+    x_host is a 2-D CPU tensor of fp16 values (float16, or int16/uint16 bit patterns),
+    ideally pinned; out_host, if given, is a (values, indices) pair of CPU tensors
+    [seg_num, k] (int16/float16 and int32).  Everything is queued on `stream` and this call
+    returns after the results are on the host."""
+    dev = torch.device(device or "cuda")
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
+    seg_num, seg_len = x_host.shape
+    key = (dev.index, s.cuda_stream)
+    buf = _staging.get(key)
+    if buf is None or buf.numel() < x_host.numel():
+        buf = torch.empty(x_host.numel(), dtype=torch.float16, device=dev)
+        _staging[key] = buf
+    xd = buf[: x_host.numel()].view(seg_num, seg_len)
+    with torch.cuda.stream(s):
+        xd.view(torch.int16).copy_(x_host.view(torch.int16), non_blocking=True)
+        vals, idx = topk(xd, k, workspace=workspace, stream=s)
+        if out_host is None:
+            out_host = (torch.empty((seg_num, k), dtype=torch.float16).pin_memory(),
+                        torch.empty((seg_num, k), dtype=torch.int32).pin_memory())
+        hv, hi = out_host
+        hv.view(torch.int16).copy_(vals.view(torch.int16), non_blocking=True)
+        hi.copy_(idx, non_blocking=True)
+    s.synchronize()
+    return hv, hi

@@ -60,9 +60,11 @@ size_t bt_topk_half_segmented_workspace_size(int seg_num, long long max_total_le
 
 /* Reads back (synchronously, on `stream`) the device status word of the last call that used
  * this workspace: 0 when every device-side check passed, otherwise a bitwise OR of
- * BT_STATUS_* flags.  stats (may be NULL) receives 4 counters: chunks that needed the exact
- * local select, chunks that reused a published threshold, chunks that ran the group-max
- * select, and segments merged. */
+ * BT_STATUS_* flags.  stats (may be NULL) receives BT_STATS_WORDS counters, filled only when
+ * the process runs with BT_STATS=1: chunks that needed the exact local select, chunks with no
+ * candidate, group-max threshold selects, rows emitted, first chunks whose threshold was the
+ * previous segment's (verified), and one reserved word. */
+#define BT_STATS_WORDS 6
 #define BT_STATUS_OK 0
 #define BT_STATUS_WAIT_TIMEOUT 1    /* a bulk-copy wait hit its iteration cap */
 #define BT_STATUS_BAD_OFFSETS 2     /* CSR offsets decreasing or beyond max_total_len */
@@ -74,6 +76,12 @@ int bt_workspace_status(const void* d_workspace, int seg_num, void* stream, unsi
  * ev_start just before its main (streaming) kernel and ev_stop just after it, on the call's
  * stream.  Pass NULLs to switch it off.  Process-wide; not for concurrent callers. */
 void bt_set_profile_events(void* ev_start, void* ev_stop);
+
+/* Launch facts for the current device (initialises the per-device set-up on first use):
+ * info[0..5] = {SM count, resident blocks per SM for k <= 128, for k > 128, dynamic shared
+ * memory bytes per block for k <= 128, for k > 128, threads per block}.  Writes min(n, 6)
+ * entries; returns a cudaError_t code. */
+int bt_device_info(int* info, int n);
 
 /* Human-readable text for a return code or status flag set. */
 const char* bt_error_string(int code);
