@@ -24,7 +24,8 @@ constexpr int kMergeThreads = 256;
 constexpr int kMaxChunksPerSegment = 4097;            // 2^26 values, misaligned start
 constexpr uint32_t kNoThreshold = 0xFFFFu;  // key bound that admits every value, NaN too
 constexpr uint32_t kFewerThanK = 0x10000u;  // "fewer than k candidates": all of them qualify
-constexpr uint32_t kWaitCap = 1u << 24;               // bounded mbarrier polling
+constexpr uint32_t kWaitCap = 1u << 16;               // bounded mbarrier waits
+constexpr uint32_t kWaitHintNs = 20000;               // per-try suspend limit
 
 // status word bits (mirrors BT_STATUS_* in include/batch_topk_b200.h)
 constexpr uint32_t kStatusWaitTimeout = 1;
@@ -132,17 +133,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
+  // The suspend-time hint lets the thread sleep until the phase completes (or the hint
+  // expires) instead of polling and taking issue slots from the working warps.
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kWaitHintNs)
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait: returns false if the phase did not complete within kWaitCap polls.
+// Bounded wait: returns false if the phase did not complete within kWaitCap tries (each
+// try suspends for at most kWaitHintNs, so the bound is about a second).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   for (uint32_t it = 0; it < kWaitCap; ++it) {
     if (mbar_try_wait(bar, parity)) return true;

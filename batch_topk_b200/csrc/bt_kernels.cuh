@@ -123,7 +123,7 @@ struct alignas(16) Scratch {
   alignas(16) uint32_t gkeys[Cfg<BIG>::kGroupWords * kThreads];  // 128-bit reads
   uint32_t coff[Cfg<BIG>::kCoffCap + 1];
   uint32_t warp_tot[kWarps];
-  uint32_t wcnt[2][kWarps];  // per-warp candidate counts, double-buffered by chunk parity
+  alignas(16) uint32_t wcnt[2][kWarps];  // per-warp candidate counts, double-buffered
   int bin1, bin2;
   uint32_t before1, before2;
   uint32_t bcast[4];
@@ -158,7 +158,7 @@ struct alignas(16) Scratch<false> {
   unsigned long long kpub;                 // merger: (segment << 32) | k-th key
   alignas(16) uint32_t gkeys[Cfg<false>::kGroupWords * kThreads];  // 128-bit reads
   uint32_t warp_tot[kWarps];
-  uint32_t wcnt[2][kWarps];
+  alignas(16) uint32_t wcnt[2][kWarps];  // per-warp candidate counts (128-bit reads)
   uint32_t kuse[2];
   int bin1, bin2;
   uint32_t before1, before2;
@@ -169,7 +169,8 @@ using SmallScratch = Scratch<false>;
 
 // Every array read with 128-bit shared loads (lds128) must start on a 16-byte boundary.
 static_assert(offsetof(Scratch<false>, hist1) % 16 == 0 && offsetof(Scratch<false>, hist2) % 16 == 0 &&
-              offsetof(Scratch<false>, gkeys) % 16 == 0, "16-byte alignment of lds128 operands");
+              offsetof(Scratch<false>, gkeys) % 16 == 0 && offsetof(Scratch<false>, wcnt) % 16 == 0,
+              "16-byte alignment of lds128 operands");
 static_assert(offsetof(Scratch<true>, hist1) % 16 == 0 && offsetof(Scratch<true>, hist2) % 16 == 0 &&
               offsetof(Scratch<true>, gkeys) % 16 == 0, "16-byte alignment of lds128 operands");
 
@@ -212,10 +213,11 @@ __device__ void producer_loop(const TopkParams& p, long long q0, long long q1, u
     cs = lo;
   }
   long long issued = 0;
+  int st = 0;     // stage of the next load
+  int round = 0;  // how many times every stage has been filled
   for (long long q = q0; q < q1; ++q, ++issued) {
-    const int st = static_cast<int>(issued % S);
-    if (issued >= S) {
-      if (!mbar_wait(&empty[st], static_cast<uint32_t>(((issued / S) - 1) & 1))) {
+    if (round > 0) {  // wait until the consumers released this stage's previous use
+      if (!mbar_wait(&empty[st], static_cast<uint32_t>((round - 1) & 1))) {
         atomicOr(&p.status[0], kStatusWaitTimeout);
         break;
       }
@@ -265,6 +267,10 @@ __device__ void producer_loop(const TopkParams& p, long long q0, long long q1, u
                 static_cast<uint32_t>(si.nvc) * 16u, &full[st], policy);
     } else {
       mbar_arrive(&full[st]);
+    }
+    if (++st == S) {
+      st = 0;
+      ++round;
     }
   }
   // Do not retire while a bulk copy may still land in this block's shared memory.
@@ -418,9 +424,26 @@ __device__ __forceinline__ uint32_t thread_flags(const StageInfo& si, const uint
                     (si.vhi >= vbase && si.vhi < vbase + kVecPerThread);
   uint32_t flags = 0, cnt = 0;
   if (!edge) {
+    if (vbase + kVecPerThread <= si.nvc) {
+      // Common case: the maximum of the thread's 64 values (max ignores NaN, which never
+      // passes) against the threshold; exact masks only when something passes.
+      __half2 acc = u32_as_h2(0x7E007E00u);
+#pragma unroll
+      for (int jj = 0; jj < kVecPerThread; ++jj) {
+        const uint4 w = lds128(buf + (vbase + (jj ^ sw)) * 16);  // rotated: conflict-free
+        const __half2 m01 = __hmax2(u32_as_h2(w.x), u32_as_h2(w.y));
+        const __half2 m23 = __hmax2(u32_as_h2(w.z), u32_as_h2(w.w));
+        acc = __hmax2(acc, __hmax2(m01, m23));
+      }
+      const uint32_t hit = STRICT ? __hgt2_mask(acc, v2) : __hge2_mask(acc, v2);
+      if (hit == 0) {
+        *count = 0;
+        return 0;
+      }
+    }
 #pragma unroll
     for (int jj = 0; jj < kVecPerThread; ++jj) {
-      const int j = jj ^ sw;  // rotated read order: conflict-free 16-byte smem reads
+      const int j = jj ^ sw;
       const int vi = vbase + j;
       if (vi < si.nvc) {
         const uint4 w = lds128(buf + vi * 16);

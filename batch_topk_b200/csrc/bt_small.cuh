@@ -33,26 +33,31 @@ __device__ __forceinline__ Counted count_chunk(const StageInfo& si, const uint8_
   const __half2 v2 = u32_as_h2(vb | (vb << 16));
   Counted c;
   c.flags = thread_flags<STRICT>(si, buf, v2, take_all, &c.cnt);
-  uint32_t incl = c.cnt;
+  uint32_t incl = 0;
+  if (__ballot_sync(0xFFFFFFFFu, c.cnt != 0)) {  // warp scan only when something passed
+    incl = c.cnt;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-    if (lane >= o) incl += y;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
   }
   if (lane == 31) sm.wcnt[par][warp] = incl;
-  if (tid == 0) {
+  if (tid == kThreads - 1) {  // the last warp has the fewest vectors: it stages the threshold
     const unsigned long long kp = *reinterpret_cast<volatile unsigned long long*>(&sm.kpub);
     sm.kuse[par] = (static_cast<int>(kp >> 32) == seg) ? static_cast<uint32_t>(kp & 0xFFFFu)
                                                        : kNoThreshold;
   }
   csync();
   c.fail = sm.fail != 0;
+  const uint4 wa = lds128(&sm.wcnt[par][0]);
+  const uint4 wb = lds128(&sm.wcnt[par][4]);
+  const uint32_t t[kWarps] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
   uint32_t total = 0, wpre = 0;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) {
-    const uint32_t t = sm.wcnt[par][w];
-    wpre += w < warp ? t : 0u;
-    total += t;
+    wpre += w < warp ? t[w] : 0u;
+    total += t[w];
   }
   c.total = total;
   c.base = wpre + incl - c.cnt;
@@ -100,8 +105,9 @@ __device__ __forceinline__ void send_batch(SmallScratch& sm, int b, const BatchM
 
 // One non-empty chunk: threshold, count, write the batch, hand it to the merger.
 __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
-                           SmallScratch& sm, SegState& ss, int par, long long nb,
+                           SmallScratch& sm, SegState& ss, int par, long long* nbp,
                            uint32_t* guess) {
+  const long long nb = *nbp;
   const uint32_t k = static_cast<uint32_t>(p.k);
   const uint32_t cap = static_cast<uint32_t>(p.cap);
   uint32_t K = ss.K;
@@ -169,7 +175,8 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
       written = true;
     }
   }
-  if (!written) {
+  const bool send = n > 0 || si.last;  // empty middle chunks need no hand-off
+  if (!written && send) {
     if (!wait_batch_free(sm, nb)) return kChunkFail;
     if (c.flags) {
       if (strict) write_batch<true>(si, buf, c.flags, K, c.base, sm.batch[b]);
@@ -186,6 +193,8 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
     ss.K = c.knext;
     ss.strict = true;
   }
+  if (threadIdx.x == 0 && p.stats && n == 0) atomicAdd(&p.status[2], 1u);
+  if (!send) return kChunkDone;
   BatchMeta meta;
   meta.len = si.a1 - si.a0;
   meta.part_slot = ss.slot0;
@@ -197,7 +206,7 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
   meta.nchunks = si.nchunks;
   meta.K = ss.K;
   send_batch(sm, b, meta);
-  if (threadIdx.x == 0 && p.stats && n == 0) atomicAdd(&p.status[2], 1u);
+  *nbp = nb + 1;
   return kChunkDone;
 }
 
@@ -208,31 +217,33 @@ __device__ void consumer_loop_small(const TopkParams& p, long long q0, long long
   SegState ss;
   uint32_t guess = kNoThreshold;
   long long nb = 0;  // batches sent
-  long long i = 0;
+  int st = 0, par = 0;
+  uint32_t ph = 0;   // full-barrier phase parity of stage st
   bool failed = false;
-  for (long long q = q0; q < q1; ++q, ++i) {
-    const int st = static_cast<int>(i % S);
-    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>((i / S) & 1));
+  for (long long q = q0; q < q1; ++q) {
+    const bool ok = mbar_wait(&full[st], ph);
     if (!ok) sm.fail = 1u;
     const StageInfo& si = info[st];  // read in place: valid until this stage is released
-    if (si.nvc == 0) {
-      release_stage(&empty[st]);
-      continue;
+    if (si.nvc > 0) {
+      if (si.s != ss.s) {
+        ss = SegState{};
+        ss.s = si.s;
+        ss.slot0 = si.slot;  // first slot of this block's part of the segment
+      }
+      const int r = small_chunk(p, si, stages + static_cast<size_t>(st) * kStageBytes, sm, ss,
+                                par, &nb, &guess);
+      if (r == kChunkFail) {
+        failed = true;
+        break;
+      }
+      ++ss.mycnt;
+      par ^= 1;
     }
-    if (si.s != ss.s) {
-      ss = SegState{};
-      ss.s = si.s;
-      ss.slot0 = si.slot;  // first slot of this block's part of the segment
-    }
-    const int r = small_chunk(p, si, stages + static_cast<size_t>(st) * kStageBytes, sm, ss,
-                              static_cast<int>(i & 1), nb, &guess);
-    if (r == kChunkFail) {
-      failed = true;
-      break;
-    }
-    ++ss.mycnt;
-    ++nb;
     release_stage(&empty[st]);
+    if (++st == S) {
+      st = 0;
+      ph ^= 1u;
+    }
   }
   // tell the merger to stop (bounded wait for the buffer)
   wait_batch_free(sm, nb);
