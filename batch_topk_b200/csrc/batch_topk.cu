@@ -36,7 +36,7 @@ long long csr_slot_bound(long long seg_num, long long total_len) {
 }
 
 struct Layout {
-  size_t status, thresh, done, chunk_start, counts, offs, cand, total;
+  size_t status, thresh, done, chunk_start, part_start, counts, offs, cand, total;
 };
 
 // status | seg_thresh | seg_done | chunk_start (CSR) | chunk_count | chunk_off | candidates,
@@ -53,6 +53,7 @@ Layout make_layout(long long seg_num, long long slots, int cap, bool csr) {
   L.thresh = take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
   L.done = take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
   L.chunk_start = csr ? take(static_cast<size_t>(seg_num + 1) * sizeof(uint32_t)) : 0;
+  L.part_start = csr ? take(static_cast<size_t>(seg_num + 1) * sizeof(uint32_t)) : 0;
   L.counts = take(static_cast<size_t>(slots) * sizeof(uint32_t));
   L.offs = take(static_cast<size_t>(slots + 1) * sizeof(uint32_t));
   L.cand = take(static_cast<size_t>(slots) * cap * sizeof(uint32_t));
@@ -80,6 +81,17 @@ std::mutex g_mu;
 DeviceInfo g_dev[64];
 cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
 int g_stats = -1;
+int g_part_chunks_env = -1;  // BT_PART_CHUNKS override of the work-part size (0: automatic)
+
+// Chunks per work part: about three parts per resident block, so blocks that run ahead take
+// more parts, while a part stays long enough to amortise its first-chunk threshold.
+int choose_part_chunks(long long total_chunks, long long resident) {
+  if (g_part_chunks_env > 0) return g_part_chunks_env;
+  long long u = total_chunks / (3 * resident);
+  if (u < 1) u = 1;
+  if (u > 64) u = 64;
+  return static_cast<int>(u);
+}
 
 cudaError_t device_info(DeviceInfo* out) {
   int dev = 0;
@@ -110,6 +122,10 @@ cudaError_t device_info(DeviceInfo* out) {
       const char* s = std::getenv("BT_STATS");
       g_stats = (s && s[0] == '1') ? 1 : 0;
     }
+    if (g_part_chunks_env < 0) {
+      const char* s = std::getenv("BT_PART_CHUNKS");
+      g_part_chunks_env = s ? std::atoi(s) : 0;
+    }
     d.ready = true;
   }
   *out = d;
@@ -121,6 +137,15 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
   cudaError_t e = device_info(&di);
   if (e != cudaSuccess) return e;
   p.stats = g_stats > 0 ? 1 : 0;
+  const bool big = p.k > Cfg<false>::kSelCap;
+  const long long resident = static_cast<long long>(di.sms) * di.blocks_per_sm[big ? 1 : 0];
+  p.part_chunks = choose_part_chunks(work_items, resident);
+  long long parts = work_items;  // CSR: an upper bound (every part holds a chunk)
+  if (!csr) {
+    const long long per = (p.p_max + p.part_chunks - 1) / p.part_chunks;
+    p.parts_total = static_cast<long long>(p.seg_num) * per;
+    parts = p.parts_total;
+  }
   if (csr) {
     csr_prep_kernel<<<1, 1024, 0, stream>>>(p);
   } else {
@@ -129,14 +154,12 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const bool big = p.k > Cfg<false>::kSelCap;
-  const long long resident = static_cast<long long>(di.sms) * di.blocks_per_sm[big ? 1 : 0];
-  const int grid = static_cast<int>(work_items < resident ? (work_items > 0 ? work_items : 1) : resident);
+  const int grid = static_cast<int>(parts < resident ? (parts > 0 ? parts : 1) : resident);
   if (g_prof_start) cudaEventRecord(g_prof_start, stream);
   if (big) {
-    topk_kernel<true><<<grid, block_threads<true>(), SmemLayout<true>::bytes, stream>>>(p, work_items);
+    topk_kernel<true><<<grid, block_threads<true>(), SmemLayout<true>::bytes, stream>>>(p);
   } else {
-    topk_kernel<false><<<grid, block_threads<false>(), SmemLayout<false>::bytes, stream>>>(p, work_items);
+    topk_kernel<false><<<grid, block_threads<false>(), SmemLayout<false>::bytes, stream>>>(p);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -160,6 +183,7 @@ TopkParams base_params(const void* d_input, int seg_num, int k, void* d_out_valu
   p.seg_thresh = reinterpret_cast<uint32_t*>(ws + L.thresh);
   p.seg_done = reinterpret_cast<uint32_t*>(ws + L.done);
   p.chunk_start = reinterpret_cast<uint32_t*>(ws + L.chunk_start);
+  p.part_start = reinterpret_cast<uint32_t*>(ws + L.part_start);
   p.chunk_count = reinterpret_cast<uint32_t*>(ws + L.counts);
   p.chunk_off = reinterpret_cast<uint32_t*>(ws + L.offs);
   p.cand = reinterpret_cast<uint32_t*>(ws + L.cand);

@@ -48,7 +48,10 @@ struct TopkParams {
   const int* offsets;            // CSR offsets (seg_num + 1) or nullptr
   int p_max;                     // fixed-length: chunk slots per segment
   uint32_t* chunk_start;         // CSR: first slot of each segment (seg_num + 1)
+  uint32_t* part_start;          // CSR: first work part of each segment (seg_num + 1)
   long long slot_capacity;       // chunk slots in the workspace
+  long long parts_total;         // fixed-length: number of work parts
+  int part_chunks;               // at most this many chunks per work part
   int k;
   int groups;                    // group maxima per thread in the threshold select
   int cap;                       // candidate capacity per chunk slot
@@ -111,8 +114,11 @@ struct StageInfo {
   int nchunks;     // chunks of the segment
   int chunk_vecs;
   int vlo, vhi;    // chunk-relative vectors that straddle the segment ends (-1: none)
-  int last;        // last chunk of this segment in this block's range
+  int last;        // last chunk of this work part
+  int part;        // work part id (kStopPart: no more work)
 };
+constexpr int kStopPart = -1;
+constexpr uint32_t kWorkCounter = 8;  // status[8]: next work part to claim (reset per call)
 
 template <bool BIG>
 struct alignas(16) Scratch {
@@ -195,69 +201,55 @@ __device__ __forceinline__ void csync() { group_sync<kThreads>(); }
 
 // ---- producer ------------------------------------------------------------------------
 
-template <bool BIG>
-__device__ void producer_loop(const TopkParams& p, long long q0, long long q1, uint8_t* stages,
-                              uint64_t* full, uint64_t* empty, StageInfo* info) {
-  constexpr int S = Cfg<BIG>::kStagesN;
-  const uint64_t policy = policy_evict_first();
-  int s = -1;
-  SegGeom g{};
-  long long slot0 = 0;
-  int cs = 0;  // CSR: segment cursor
-  if (p.offsets && q0 < q1) {
-    int lo = 0, hi = p.seg_num;  // chunk_start[lo] <= q0 < chunk_start[hi]
+// Work parts: each segment's chunks are cut into ceil(nchunks / part_chunks) parts of
+// near-equal size; blocks claim parts dynamically, in segment order.
+__device__ __forceinline__ long long total_parts(const TopkParams& p) {
+  return p.offsets ? static_cast<long long>(p.part_start[p.seg_num]) : p.parts_total;
+}
+
+// Part id -> segment and chunk range [*c0, *c1).
+__device__ __forceinline__ void decode_part(const TopkParams& p, long long part, int* s, int* c0,
+                                            int* c1, SegGeom* g, long long* slot0) {
+  int seg, j, pps;
+  if (!p.offsets) {
+    const int per = (p.p_max + p.part_chunks - 1) / p.part_chunks;
+    seg = static_cast<int>(part / per);
+    j = static_cast<int>(part - static_cast<long long>(seg) * per);
+    pps = per;
+    *slot0 = static_cast<long long>(seg) * p.p_max;
+  } else {
+    int lo = 0, hi = p.seg_num;  // part_start[lo] <= part < part_start[hi]
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
-      if (static_cast<long long>(p.chunk_start[mid]) <= q0) lo = mid; else hi = mid;
+      if (static_cast<long long>(p.part_start[mid]) <= part) lo = mid; else hi = mid;
     }
-    cs = lo;
+    seg = lo;
+    j = static_cast<int>(part - p.part_start[lo]);
+    pps = static_cast<int>(p.part_start[lo + 1] - p.part_start[lo]);
+    *slot0 = static_cast<long long>(p.chunk_start[seg]);
   }
+  *g = seg_geom(p, seg);
+  const int n = g->nchunks;
+  *s = seg;
+  *c0 = static_cast<int>(static_cast<long long>(j) * n / pps);
+  *c1 = static_cast<int>(static_cast<long long>(j + 1) * n / pps);
+}
+
+template <bool BIG>
+__device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* full,
+                              uint64_t* empty, StageInfo* info) {
+  constexpr int S = Cfg<BIG>::kStagesN;
+  const uint64_t policy = policy_evict_first();
+  const long long nparts = total_parts(p);
   long long issued = 0;
   int st = 0;     // stage of the next load
   int round = 0;  // how many times every stage has been filled
-  for (long long q = q0; q < q1; ++q, ++issued) {
-    if (round > 0) {  // wait until the consumers released this stage's previous use
-      if (!mbar_wait(&empty[st], static_cast<uint32_t>((round - 1) & 1))) {
-        atomicOr(&p.status[0], kStatusWaitTimeout);
-        break;
-      }
-    }
-    int sn, c;
-    if (!p.offsets) {
-      sn = static_cast<int>(q / p.p_max);
-      c = static_cast<int>(q - static_cast<long long>(sn) * p.p_max);
-    } else {
-      while (cs + 1 < p.seg_num && static_cast<long long>(p.chunk_start[cs + 1]) <= q) ++cs;
-      sn = cs;
-      c = static_cast<int>(q - p.chunk_start[cs]);
-    }
-    if (sn != s) {
-      s = sn;
-      g = seg_geom(p, s);
-      slot0 = q - c;
-    }
-    StageInfo si;
-    si.s = s;
-    si.c = c;
-    si.slot = slot0 + c;
-    si.a0 = g.a0;
-    si.a1 = g.a1;
-    si.v0 = g.v0;
-    si.nchunks = g.nchunks;
-    si.chunk_vecs = g.chunk_vecs;
-    si.last = (c == g.nchunks - 1 || q + 1 == q1) ? 1 : 0;
-    if (c >= g.nchunks) {
-      si.nvc = 0;
-      si.cv0 = 0;
-      si.vlo = si.vhi = -1;
-    } else {
-      si.cv0 = g.v0 + static_cast<long long>(c) * g.chunk_vecs;
-      const long long rem = g.v0 + g.nv - si.cv0;
-      si.nvc = static_cast<int>(rem < g.chunk_vecs ? rem : g.chunk_vecs);
-      const long long first = g.v0 - si.cv0;
-      const long long last = ((g.a1 - 1) >> 3) - si.cv0;
-      si.vlo = ((g.a0 & 7) && first >= 0 && first < si.nvc) ? static_cast<int>(first) : -1;
-      si.vhi = ((g.a1 & 7) && last >= 0 && last < si.nvc) ? static_cast<int>(last) : -1;
+  bool ok = true;
+  // one stage: wait for it to be free, fill its info, start the copy (or just signal)
+  auto put = [&](const StageInfo& si) -> bool {
+    if (round > 0 && !mbar_wait(&empty[st], static_cast<uint32_t>((round - 1) & 1))) {
+      atomicOr(&p.status[0], kStatusWaitTimeout);
+      return false;
     }
     info[st] = si;
     if (si.nvc > 0) {
@@ -268,10 +260,49 @@ __device__ void producer_loop(const TopkParams& p, long long q0, long long q1, u
     } else {
       mbar_arrive(&full[st]);
     }
+    ++issued;
     if (++st == S) {
       st = 0;
       ++round;
     }
+    return true;
+  };
+  long long part = atomicAdd(&p.status[kWorkCounter], 1u);
+  while (ok && part < nparts) {
+    const long long next = atomicAdd(&p.status[kWorkCounter], 1u);  // claim ahead
+    int s, c0, c1;
+    SegGeom g;
+    long long slot0;
+    decode_part(p, part, &s, &c0, &c1, &g, &slot0);
+    for (int c = c0; c < c1 && ok; ++c) {
+      StageInfo si;
+      si.s = s;
+      si.c = c;
+      si.part = static_cast<int>(part);
+      si.slot = slot0 + c;
+      si.a0 = g.a0;
+      si.a1 = g.a1;
+      si.v0 = g.v0;
+      si.nchunks = g.nchunks;
+      si.chunk_vecs = g.chunk_vecs;
+      si.last = c == c1 - 1 ? 1 : 0;
+      si.cv0 = g.v0 + static_cast<long long>(c) * g.chunk_vecs;
+      const long long rem = g.v0 + g.nv - si.cv0;
+      si.nvc = static_cast<int>(rem < g.chunk_vecs ? rem : g.chunk_vecs);
+      const long long first = g.v0 - si.cv0;
+      const long long last = ((g.a1 - 1) >> 3) - si.cv0;
+      si.vlo = ((g.a0 & 7) && first >= 0 && first < si.nvc) ? static_cast<int>(first) : -1;
+      si.vhi = ((g.a1 & 7) && last >= 0 && last < si.nvc) ? static_cast<int>(last) : -1;
+      ok = put(si);
+    }
+    part = next;
+  }
+  if (ok) {  // the stop sentinel
+    StageInfo z{};
+    z.s = -1;
+    z.part = kStopPart;
+    z.vlo = z.vhi = -1;
+    ok = put(z);
   }
   // Do not retire while a bulk copy may still land in this block's shared memory.
   for (long long r = issued - S; r < issued; ++r) {
@@ -290,6 +321,7 @@ __device__ __forceinline__ void release_stage(uint64_t* empty) {
 
 struct SegState {
   int s = -1;
+  int part = -2;              // work part (kStopPart never matches: -2)
   uint32_t K = kNoThreshold;  // current threshold key (desc)
   bool strict = false;        // later chunks need key < K
   bool spilled = false;       // the shared-memory candidate buffer overflowed
@@ -996,34 +1028,34 @@ __device__ void close_segment(const TopkParams& p, const SegState& ss, Scratch<B
 }
 
 template <bool BIG>
-__device__ void consumer_loop(const TopkParams& p, long long q0, long long q1, uint8_t* stages,
-                              uint64_t* full, uint64_t* empty, const StageInfo* info,
-                              Scratch<BIG>& sm) {
+__device__ void consumer_loop(const TopkParams& p, uint8_t* stages, uint64_t* full,
+                              uint64_t* empty, const StageInfo* info, Scratch<BIG>& sm) {
   constexpr int S = Cfg<BIG>::kStagesN;
   SegState ss;
-  long long i = 0;
-  for (long long q = q0; q < q1; ++q, ++i) {
-    const int st = static_cast<int>(i % S);
-    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>((i / S) & 1));
+  int st = 0, par = 0;
+  uint32_t ph = 0;
+  for (;;) {
+    const bool ok = mbar_wait(&full[st], ph);
     if (!ok) sm.fail = 1u;
     const StageInfo& si = info[st];  // read in place: valid until this stage is released
     const uint8_t* buf = stages + static_cast<size_t>(st) * kStageBytes;
-    const int par = static_cast<int>(i & 1);
     int r = kChunkDone;
-    if (si.s == ss.s && ss.strict && si.nvc > 0) {
+    if (si.part == ss.part && ss.strict && si.nvc > 0) {  // uniform: stage info is shared
       // steady state: one barrier per chunk, usually nothing to write
       r = stream_chunk<true, BIG>(p, si, buf, sm, ss, par);
       if (r == kChunkOverflow) r = first_chunk<BIG>(p, si, buf, sm, ss, par);  // values ramped up
     } else {
       if (group_or<kThreads>(!ok)) r = kChunkFail;
       if (r != kChunkFail) {
-        if (si.s != ss.s) {
+        if (si.part != ss.part) {
           close_segment<BIG>(p, ss, sm);
+          if (si.part == kStopPart) break;
           ss = SegState{};
           ss.s = si.s;
+          ss.part = si.part;
           ss.nchunks = si.nchunks;
           ss.chunk_vecs = si.chunk_vecs;
-          ss.slot0 = si.slot - si.c;
+          ss.slot0 = si.slot - si.c;  // the segment's chunk 0 (the global merge walks all)
           ss.v0 = si.v0;
           ss.a0 = si.a0;
           ss.a1 = si.a1;
@@ -1035,10 +1067,16 @@ __device__ void consumer_loop(const TopkParams& p, long long q0, long long q1, u
       if (threadIdx.x == 0) atomicOr(&p.status[0], kStatusWaitTimeout);
       return;
     }
-    if (si.nvc > 0) ++ss.mycnt;
+    if (si.nvc > 0) {
+      ++ss.mycnt;
+      par ^= 1;
+    }
     release_stage(&empty[st]);
+    if (++st == S) {
+      st = 0;
+      ph ^= 1u;
+    }
   }
-  close_segment<BIG>(p, ss, sm);
 }
 
 }  // namespace bt
@@ -1050,7 +1088,7 @@ namespace bt {
 // 96 registers: each SM sub-partition (16K registers) holds 5 warps, so two 9-warp blocks fit.
 template <bool BIG>
 __global__ void __maxnreg__(96)
-topk_kernel(TopkParams p, long long work_total) {
+topk_kernel(TopkParams p) {
   using L = SmemLayout<BIG>;
   constexpr int S = L::S;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -1061,13 +1099,6 @@ topk_kernel(TopkParams p, long long work_total) {
   StageInfo* info = reinterpret_cast<StageInfo*>(smem + L::off_info);
   const int tid = threadIdx.x;
 
-  long long W = work_total;
-  if (p.offsets) {
-    const long long t = static_cast<long long>(p.chunk_start[p.seg_num]);
-    W = t < p.slot_capacity ? t : p.slot_capacity;
-  }
-  const long long q0 = W * blockIdx.x / gridDim.x;
-  const long long q1 = W * (blockIdx.x + 1) / gridDim.x;
   if (tid == 0) {
     if constexpr (!BIG) {
       for (int b = 0; b < 2; ++b) {
@@ -1081,8 +1112,9 @@ topk_kernel(TopkParams p, long long work_total) {
       mbar_init(&empty[st], kWarps);  // one arrival per consumer warp
       StageInfo z{};
       z.s = -1;
+      z.part = kStopPart;
       z.vlo = z.vhi = -1;
-      info[st] = z;  // a wait that times out then sees an empty item, never garbage
+      info[st] = z;  // a wait that times out then sees the stop item, never garbage
     }
     fence_mbar_init();
     sm.fail = 0u;
@@ -1094,16 +1126,16 @@ topk_kernel(TopkParams p, long long work_total) {
   __syncthreads();
   if (tid >= kThreads) {
     if (tid == kThreads) {
-      producer_loop<BIG>(p, q0, q1, stages, full, empty, info);
+      producer_loop<BIG>(p, stages, full, empty, info);
     } else if (!BIG && tid >= kThreads + 32) {
       if constexpr (!BIG) merger_loop(p, sm);
     }
     return;
   }
   if constexpr (BIG) {
-    consumer_loop<true>(p, q0, q1, stages, full, empty, info, sm);
+    consumer_loop<true>(p, stages, full, empty, info, sm);
   } else {
-    consumer_loop_small(p, q0, q1, stages, full, empty, info, sm);
+    consumer_loop_small(p, stages, full, empty, info, sm);
   }
 }
 
@@ -1126,7 +1158,7 @@ __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
   const int tid = threadIdx.x;
   if (tid < 16) p.status[tid] = 0;
   __syncthreads();
-  uint32_t carry = 0;
+  uint32_t carry = 0, pcarry = 0;
   for (int base = 0; base < p.seg_num; base += 1024) {
     const int s = base + tid;
     uint32_t nch = 0;
@@ -1148,10 +1180,18 @@ __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
     const uint32_t pre = block_excl_scan<1024>(nch, &tot, warp_tot);
     if (s < p.seg_num) p.chunk_start[s] = carry + pre;
     carry += tot;
+    const uint32_t npart = (nch + p.part_chunks - 1) / p.part_chunks;
+    uint32_t ptot;
+    const uint32_t ppre = block_excl_scan<1024>(npart, &ptot, warp_tot);
+    if (s < p.seg_num) p.part_start[s] = pcarry + ppre;
+    pcarry += ptot;
   }
   if (tid == 0) {
     p.chunk_start[p.seg_num] = carry;
-    if (static_cast<long long>(carry) > p.slot_capacity) atomicOr(&p.status[0], kStatusBadOffsets);
+    // chunks beyond the workspace capacity: process no part at all and flag the call
+    const bool over = static_cast<long long>(carry) > p.slot_capacity;
+    p.part_start[p.seg_num] = over ? 0u : pcarry;
+    if (over) atomicOr(&p.status[0], kStatusBadOffsets);
   }
 }
 

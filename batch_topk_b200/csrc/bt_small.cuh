@@ -210,9 +210,8 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
   return kChunkDone;
 }
 
-__device__ void consumer_loop_small(const TopkParams& p, long long q0, long long q1,
-                                    uint8_t* stages, uint64_t* full, uint64_t* empty,
-                                    const StageInfo* info, SmallScratch& sm) {
+__device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64_t* full,
+                                    uint64_t* empty, const StageInfo* info, SmallScratch& sm) {
   constexpr int S = Cfg<false>::kStagesN;
   SegState ss;
   uint32_t guess = kNoThreshold;
@@ -220,15 +219,18 @@ __device__ void consumer_loop_small(const TopkParams& p, long long q0, long long
   int st = 0, par = 0;
   uint32_t ph = 0;   // full-barrier phase parity of stage st
   bool failed = false;
-  for (long long q = q0; q < q1; ++q) {
-    const bool ok = mbar_wait(&full[st], ph);
-    if (!ok) sm.fail = 1u;
+  for (;;) {
+    // A failed wait is noticed by everyone at the next barrier (sm.fail), so every consumer
+    // thread keeps taking the same branches; stage info is never garbage (initialised).
+    if (!mbar_wait(&full[st], ph)) sm.fail = 1u;
     const StageInfo& si = info[st];  // read in place: valid until this stage is released
+    if (si.part == kStopPart) break;
     if (si.nvc > 0) {
-      if (si.s != ss.s) {
+      if (si.part != ss.part) {
         ss = SegState{};
         ss.s = si.s;
-        ss.slot0 = si.slot;  // first slot of this block's part of the segment
+        ss.part = si.part;
+        ss.slot0 = si.slot;  // first slot of this part
       }
       const int r = small_chunk(p, si, stages + static_cast<size_t>(st) * kStageBytes, sm, ss,
                                 par, &nb, &guess);
