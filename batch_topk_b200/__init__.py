@@ -18,6 +18,7 @@ CUDA_SUCCESS = 0
 CUDA_ERROR_INVALID_VALUE = 1
 MAX_K = 1024
 MAX_SEG_LEN = 1 << 26
+NOALLOC_SCRATCH_BYTES = 32 << 20  # BT_NOALLOC_SCRATCH_BYTES
 
 STATUS_FLAGS = {
     1: "bulk-copy wait timed out",
@@ -58,6 +59,16 @@ def batch_topk_half_segmented(d_input: int, d_offsets: int, seg_num: int, max_to
 
 def batch_topk_half_segmented_workspace_size(seg_num: int, max_total_len: int, k: int) -> int:
     return int(_lib.load().bt_topk_half_segmented_workspace_size(seg_num, max_total_len, k))
+
+
+def batch_topk_half_noalloc(d_input: int, seg_num: int, seg_len: int, k: int,
+                            d_output_values: int, d_output_indices: int, stream: int = 0) -> int:
+    """bt_topk_half_noalloc (no reference counterpart): batch_topk_half on the library's fixed
+    scratch array instead of a caller workspace, for callers that may not allocate device
+    memory at call time.  Returns cudaErrorInvalidValue when the shape's workspace exceeds
+    NOALLOC_SCRATCH_BYTES.  Calls that can overlap on the GPU share that array and race."""
+    return _lib.load().bt_topk_half_noalloc(d_input, seg_num, seg_len, k, d_output_values,
+                                            d_output_indices, stream)
 
 
 def workspace_status(d_workspace: int, seg_num: int = 0, stream: int = 0):

@@ -16,6 +16,7 @@ EXPORTED = (
     "bt_topk_half_workspace_size",
     "bt_topk_half_segmented",
     "bt_topk_half_segmented_workspace_size",
+    "bt_topk_half_noalloc",
     "bt_workspace_status",
     "bt_set_profile_events",
     "bt_device_info",
@@ -50,6 +51,8 @@ def load() -> C.CDLL:
         lib.bt_topk_half_segmented.restype = i32
         lib.bt_topk_half_segmented_workspace_size.argtypes = [i32, i64, i32]
         lib.bt_topk_half_segmented_workspace_size.restype = sz
+        lib.bt_topk_half_noalloc.argtypes = [vp, i32, i32, i32, vp, vp, vp]
+        lib.bt_topk_half_noalloc.restype = i32
         lib.bt_workspace_status.argtypes = [vp, i32, vp, C.POINTER(C.c_uint * 6)]
         lib.bt_workspace_status.restype = i32
         lib.bt_set_profile_events.argtypes = [vp, vp]

@@ -202,6 +202,39 @@ bool pointers_ok(const void* in, const void* ov, const int* oi, const void* ws) 
 }  // namespace
 }  // namespace bt
 
+// Scratch for bt_topk_half_noalloc: a fixed device array that lives as long as the module,
+// so that entry point never asks the runtime for memory.  BT_NOALLOC_SCRATCH_BYTES (32 MiB)
+// covers, for example, 1024 rows of 151936 values at k <= 128 (about 10.5 MB).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[BT_NOALLOC_SCRATCH_BYTES];
+
+namespace bt {
+namespace {
+
+void* g_noalloc_ptr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device.
+// The lookup may load this library's device code onto the device, so it runs on the first
+// call there and not on later ones.
+cudaError_t noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    if (!ptr || reinterpret_cast<uintptr_t>(ptr) % 256 != 0) return cudaErrorInvalidDevicePointer;
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace bt
+
 extern "C" {
 
 size_t bt_topk_half_workspace_size(int seg_num, int seg_len, int k) {
@@ -226,6 +259,23 @@ int bt_topk_half(const void* d_input, int seg_num, int seg_len, int k, void* d_o
   p.offsets = nullptr;
   p.p_max = static_cast<int>(p_max);
   return bt::launch_pipeline(p, false, slots, static_cast<cudaStream_t>(stream));
+}
+
+int bt_topk_half_noalloc(const void* d_input, int seg_num, int seg_len, int k,
+                         void* d_output_values, int* d_output_indices, void* stream) {
+  const size_t need = bt_topk_half_workspace_size(seg_num, seg_len, k);
+  if (need == 0 || need > BT_NOALLOC_SCRATCH_BYTES) return cudaErrorInvalidValue;
+  // Device info (shared-memory opt-in, occupancy) is set up before the scratch lookup so that
+  // both happen on the first call on a device, outside any stream capture the caller begins
+  // later.
+  bt::DeviceInfo di;
+  cudaError_t e = bt::device_info(&di);
+  if (e != cudaSuccess) return e;
+  void* scratch = nullptr;
+  e = bt::noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return e;
+  return bt_topk_half(d_input, seg_num, seg_len, k, d_output_values, d_output_indices, scratch,
+                      need, stream);
 }
 
 size_t bt_topk_half_segmented_workspace_size(int seg_num, long long max_total_len, int k) {

@@ -58,6 +58,33 @@ int bt_topk_half_segmented(const void* d_input, const int* d_offsets, int seg_nu
 
 size_t bt_topk_half_segmented_workspace_size(int seg_num, long long max_total_len, int k);
 
+/* bt_topk_half without a caller workspace; NO COUNTERPART IN THE REFERENCE, which always takes
+ * a caller-allocated workspace (include/batch_topk.cuh:10-19).
+ *
+ * Meant for callers that may not allocate device memory at the moment they need a top-k:
+ * code running inside a custom allocator or an out-of-memory handler (allocating there
+ * re-enters the allocator or fails outright), and hosts whose device-memory budget is fixed
+ * up front and accounted by someone else, such as an inference server that hands each plugin
+ * a pre-sized pool.  The call allocates nothing: its scratch is a fixed array of
+ * BT_NOALLOC_SCRATCH_BYTES in this library's device image, and the kernels reset the parts of
+ * it that must start at zero on every call.
+ *
+ * Limit: calls whose bt_topk_half_workspace_size(seg_num, seg_len, k) exceeds
+ * BT_NOALLOC_SCRATCH_BYTES (or is 0, an unsupported shape) return cudaErrorInvalidValue and
+ * launch nothing; use bt_topk_half with a workspace for those.  Other arguments and results
+ * are those of bt_topk_half.
+ *
+ * Set-up: the first call on each device (the current one) looks up the array's device
+ * address and the kernels' launch attributes; make that first call before beginning any
+ * stream capture on that device.  Later calls only launch.
+ *
+ * Concurrency: every call on a device shares the one array, so calls that can overlap on the
+ * GPU (different streams without ordering between them, or several host threads) race on it
+ * and give wrong results.  Serialise them, e.g. on a single stream. */
+#define BT_NOALLOC_SCRATCH_BYTES (32u << 20)
+int bt_topk_half_noalloc(const void* d_input, int seg_num, int seg_len, int k,
+                         void* d_output_values, int* d_output_indices, void* stream);
+
 /* Reads back (synchronously, on `stream`) the device status word of the last call that used
  * this workspace: 0 when every device-side check passed, otherwise a bitwise OR of
  * BT_STATUS_* flags.  stats (may be NULL) receives BT_STATS_WORDS counters, filled only when
