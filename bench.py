@@ -15,8 +15,10 @@ value      segments/s over all ranks, inputs resident in HBM, device-timed (CUDA
 e2e        the same metric through the public API from pinned host memory: per step the
            H2D copy of the input and the D2H copy of the values and indices are inside the
            timed region.
-roofline   the streaming kernel (bt::chunk_kernel), timed live with events recorded around
-           it by the library's profiling hook; algorithmic bytes = 2 B per input value.
+roofline   the streaming kernel (bt::topk_kernel<false>, k <= 128), timed live with events
+           recorded around it on the launching stream by the library's profiling hook;
+           algorithmic bytes = 2 B per input value (the output, 6 B per selected entry, is
+           0.2 % of it and left out).
 cpu_baseline  the reference's own CPU top-k (cpu_reference_topk, oracle/_ref) on this host's
            cores, on a bounded sample of the same workload (rank 0, N=1 only).
 """
@@ -54,7 +56,7 @@ def traffic_per_launch():
     try:
         with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
             d = json.load(f)
-        e = d["chunk_kernel"]
+        e = d["topk_kernel"]
         if e.get("workload") == WORKLOAD:
             return float(e["dram_bytes_per_launch"])
     except Exception:
@@ -317,9 +319,9 @@ def run_ours(args, rank, world, local_rank):
         },
         "effective_input_gbs": seg_total * SEG_LEN * 2 / (ms_per_step / 1e3) / 1e9,
         "pct_hbm_per_gpu": in_bytes / (ms_per_step / 1e3) / 1e9 / peak,
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": 2 * args.steps,  # init_kernel + topk_kernel per step
         "roofline": {
-            "bound": "hbm", "kernel": "bt::chunk_kernel",
+            "bound": "hbm", "kernel": "bt::topk_kernel<false>",
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
             "algorithmic_bytes_per_launch": in_bytes,
