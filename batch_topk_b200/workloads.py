@@ -223,6 +223,15 @@ def gen_c4(seg_num=None, max_len=C4_MAX_LEN, seed=None):
     return vals, off
 
 
+def gen_c4_range(s0: int, s1: int, seed=None) -> np.ndarray:
+    """Values of C4 segments [s0, s1) alone (the slice gen_c4 would hold there), so one shard
+    or a small test case regenerates without the whole 1.07 GB batch."""
+    s = seed or CONFIGS["C4"].seed
+    off = c4_offsets(seed=s)
+    b, e = int(off[s0]), int(off[s1])
+    return uniform_half(s, 0, np.arange(b, e, dtype=np.int64), -1.0, 1.0)
+
+
 def gen_c5(rows=None, seg_len=None, seed=None) -> np.ndarray:
     cfg = CONFIGS["C5"]
     L = seg_len or cfg.seg_len

@@ -8,6 +8,8 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py`` (its CPU-baseline 
                          built in place from the reference tree into ``oracle/_ref``.
 """
 from .oracle import (  # noqa: F401
+    METHOD_COUNT,
+    METHOD_SORT,
     Oracle,
     RefOracle,
     build,
