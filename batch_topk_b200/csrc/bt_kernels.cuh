@@ -2,35 +2,37 @@
 //
 // One streaming pass over HBM replaces the reference's three full reads (the high-byte and
 // low-byte histograms, src/radix_histogram.cuh, and the compaction,
-// src/candidate_compact.cuh):
+// src/candidate_compact.cuh).
 //
-// topk_kernel: persistent, 2 CTAs per SM, warp-specialised.
-//   * Producer warp (one elected lane): walks the CTA's contiguous range of chunk work items
-//     (segment-major) and streams each chunk (<= 16384 fp16 values, 32 KiB) into a shared
-//     memory stage with one cp.async.bulk (no multicast), signalling a "full" mbarrier.
+// topk_kernel<BIG>: persistent, 2 blocks per SM (96 registers a thread), warp-specialised.
+//   * Producer warp (one elected lane): claims work parts (a segment, or a run of its
+//     chunks when there are fewer segments than blocks) from a global counter, in segment
+//     order, and streams each chunk (<= 16384 fp16 values, 32 KiB) into a shared-memory
+//     stage with one cp.async.bulk (no multicast), signalling a "full" mbarrier.
 //   * 8 consumer warps, per chunk:
-//       1. threshold: on the first chunk of a segment (or when too many values survive), the
-//          k-th best of the chunk's group maxima.  Each maximum is a distinct element, so at
-//          least k elements of the chunk are >= it and every member of the segment's top-k
-//          is >= it (a certified bound; no histogram of the whole chunk is needed).
-//       2. ordered compaction: values passing the threshold are written in index order to
-//          the chunk's candidate slot as (fp16 bits << 16 | chunk-local index), from an 8-bit
-//          half2 compare mask per 16-byte vector and one exclusive scan over the block.
-//       3. after a chunk has written >= k candidates with key <= K, every later chunk of the
-//          segment in this CTA has larger indices, so it only needs keys strictly below K:
-//          ties at K can no longer win.  This keeps tie-heavy rows (all values equal, a few
-//          hundred copies of the maximum) to about k candidates per segment.
+//       1. threshold: on the first chunk of a segment the k-th best of the chunk's group
+//          maxima (a certified bound: every member of the segment's top-k is >= it), or the
+//          previous segment's threshold when it still leaves between k and `cap` values.
+//       2. candidate test: a 16-byte vector is skipped after four half2 compares against its
+//          maximum; passing vectors give an 8-bit mask, and one block scan orders them.
+//       3. strict mode: once k candidates with key <= K exist at lower indices, later
+//          chunks only need keys strictly below K (ties at K can no longer win), which keeps
+//          tie-heavy rows near k candidates.
 //       4. more than `cap` survivors: an exact local select (two 8-bit digit passes, the
 //          reference's radix_boundary_select logic) keeps exactly the chunk's k best.
 //     then release the stage on an "empty" mbarrier.
-//   * When the CTA finishes its part of a segment, the last CTA to finish (per-segment
-//     arrival counter; usually the only one) merges the segment: concatenates the chunk lists
-//     in index order, drops keys above the final threshold, finds the exact cutoff key with
-//     two 8-bit digit passes, keeps keys below it plus the first ties by index, and places
-//     each survivor at its rank by (key, index).  This is the reference's boundary select,
-//     compaction and final sort (src/radix_boundary_select.cuh, src/candidate_compact.cuh,
-//     src/final_topk50.cuh, src/final_block_sort.cuh) on ~k candidates, while the producer
-//     keeps prefetching the next chunks.
+//   * k <= 128 (bt_small.cuh): survivors go as (key, index, bits) composites to a merger
+//     warp that keeps the segment's exact running top-k in registers (bitonic merges) and
+//     publishes its k-th key back as the consumers' threshold.
+//   * k > 128: chunk lists go to the workspace; at the segment's end the block that finishes
+//     it (per-segment arrival counter) merges them: drops keys above the final threshold,
+//     finds the exact cutoff with two 8-bit digit passes, keeps keys below it plus the first
+//     ties by index, and places each survivor at its rank by (key, index).  This is the
+//     reference's boundary select, compaction and final sort (src/radix_boundary_select.cuh,
+//     src/candidate_compact.cuh, src/final_topk50.cuh, src/final_block_sort.cuh) on ~k
+//     candidates, while the producer keeps prefetching the next chunks.
+// Every wait (mbarrier, batch hand-off) has an iteration cap; on expiry the kernel sets
+// BT_STATUS_WAIT_TIMEOUT in the workspace status word and finishes without further waits.
 #pragma once
 
 #include <cstddef>
