@@ -82,6 +82,9 @@ DeviceInfo g_dev[64];
 cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
 int g_stats = -1;
 int g_part_chunks_env = -1;  // BT_PART_CHUNKS override of the work-part size (0: automatic)
+int g_tail_parts_env = -1;   // BT_TAIL_PARTS: parts per segment in the last wave (0: off)
+int g_tail_segs_env = -1;    // BT_TAIL_SEGS: segments in the last wave (0: one per resident block)
+int g_grid_env = -1;         // BT_GRID: blocks of the streaming kernel (0: automatic)
 
 // Chunks per work part: about three parts per resident block, so blocks that run ahead take
 // more parts, while a part stays long enough to amortise its first-chunk threshold.
@@ -125,6 +128,12 @@ cudaError_t device_info(DeviceInfo* out) {
     if (g_part_chunks_env < 0) {
       const char* s = std::getenv("BT_PART_CHUNKS");
       g_part_chunks_env = s ? std::atoi(s) : 0;
+      s = std::getenv("BT_TAIL_PARTS");
+      g_tail_parts_env = s ? std::atoi(s) : 0;
+      s = std::getenv("BT_TAIL_SEGS");
+      g_tail_segs_env = s ? std::atoi(s) : 0;
+      s = std::getenv("BT_GRID");
+      g_grid_env = s ? std::atoi(s) : 0;
     }
     d.ready = true;
   }
@@ -143,7 +152,17 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
   long long parts = work_items;  // CSR: an upper bound (every part holds a chunk)
   if (!csr) {
     const long long per = (p.p_max + p.part_chunks - 1) / p.part_chunks;
-    p.parts_total = static_cast<long long>(p.seg_num) * per;
+    p.tail_seg0 = p.seg_num;
+    p.tail_parts = static_cast<int>(per);
+    if (g_tail_parts_env > per && p.seg_num > 1) {
+      // the last segments in claim order are cut finer, so the final wave ends evenly
+      long long tail = g_tail_segs_env > 0 ? g_tail_segs_env : resident;
+      if (tail > p.seg_num) tail = p.seg_num;
+      p.tail_seg0 = static_cast<int>(p.seg_num - tail);
+      p.tail_parts = g_tail_parts_env < p.p_max ? g_tail_parts_env : p.p_max;
+    }
+    p.parts_total = static_cast<long long>(p.tail_seg0) * per +
+                    static_cast<long long>(p.seg_num - p.tail_seg0) * p.tail_parts;
     parts = p.parts_total;
   }
   if (csr) {
@@ -154,7 +173,9 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const int grid = static_cast<int>(parts < resident ? (parts > 0 ? parts : 1) : resident);
+  long long grid_ll = parts < resident ? (parts > 0 ? parts : 1) : resident;
+  if (g_grid_env > 0 && g_grid_env < grid_ll) grid_ll = g_grid_env;
+  const int grid = static_cast<int>(grid_ll);
   if (g_prof_start) cudaEventRecord(g_prof_start, stream);
   if (big) {
     topk_kernel<true><<<grid, block_threads<true>(), SmemLayout<true>::bytes, stream>>>(p);

@@ -54,6 +54,8 @@ struct TopkParams {
   long long slot_capacity;       // chunk slots in the workspace
   long long parts_total;         // fixed-length: number of work parts
   int part_chunks;               // at most this many chunks per work part
+  int tail_seg0;                 // fixed-length: segments from here on are cut into
+  int tail_parts;                //   tail_parts parts each (the last wave ends evenly)
   int k;
   int groups;                    // group maxima per thread in the threshold select
   int cap;                       // candidate capacity per chunk slot
@@ -215,9 +217,17 @@ __device__ __forceinline__ void decode_part(const TopkParams& p, long long part,
   int seg, j, pps;
   if (!p.offsets) {
     const int per = (p.p_max + p.part_chunks - 1) / p.part_chunks;
-    seg = static_cast<int>(part / per);
-    j = static_cast<int>(part - static_cast<long long>(seg) * per);
-    pps = per;
+    const long long head = static_cast<long long>(p.tail_seg0) * per;
+    if (part < head) {
+      seg = static_cast<int>(part / per);
+      j = static_cast<int>(part - static_cast<long long>(seg) * per);
+      pps = per;
+    } else {
+      const long long q = part - head;
+      seg = p.tail_seg0 + static_cast<int>(q / p.tail_parts);
+      j = static_cast<int>(q - static_cast<long long>(seg - p.tail_seg0) * p.tail_parts);
+      pps = p.tail_parts;
+    }
     *slot0 = static_cast<long long>(seg) * p.p_max;
   } else {
     int lo = 0, hi = p.seg_num;  // part_start[lo] <= part < part_start[hi]
@@ -332,6 +342,7 @@ struct SegState {
   int chunk_vecs = 0;
   uint32_t nbuf = 0;          // candidates of this segment in sm.cache
   uint32_t added = 0;         // candidates added since the threshold was last tightened
+  bool quiet = false;         // the previous chunk of the part sent nothing
   long long slot0 = 0, v0 = 0, a0 = 0, a1 = 0;
 };
 
@@ -343,9 +354,71 @@ __device__ __forceinline__ uint4 masked_vec(const StageInfo& si, const uint8_t* 
   return w;
 }
 
+// k-th smallest of the packed 16-bit keys a warp holds at src (words [lane * per, +per) per
+// lane; 0xFFFF keys are NaN maxima or padding), or 0xFFFF when fewer than k keys are
+// numeric.  The search runs over [min, max] of the numeric keys in 4-ary steps: three
+// independent warp counts per step instead of one dependent count per bit.
+__device__ __forceinline__ uint32_t kth_packed_keys(const uint32_t* src, int per, uint32_t k) {
+  uint32_t lo = 0xFFFFu, hi = 0u;
+  for (int i = 0; i < per; i += 4) {
+    const uint4 w = lds128(src + i);
+    const uint32_t v[8] = {w.x & 0xFFFFu, w.x >> 16, w.y & 0xFFFFu, w.y >> 16,
+                           w.z & 0xFFFFu, w.z >> 16, w.w & 0xFFFFu, w.w >> 16};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      lo = v[j] < lo ? v[j] : lo;
+      hi = (v[j] < 0xFFFFu && v[j] > hi) ? v[j] : hi;
+    }
+  }
+  lo = __reduce_min_sync(0xFFFFFFFFu, lo);
+  hi = __reduce_max_sync(0xFFFFFFFFu, hi);
+  auto count_le = [&](uint32_t m1, uint32_t m2, uint32_t m3, uint32_t* c1, uint32_t* c2,
+                      uint32_t* c3) {
+    uint32_t a = 0, b = 0, c = 0;
+    for (int i = 0; i < per; i += 4) {
+      const uint4 w = lds128(src + i);
+      const uint32_t v[8] = {w.x & 0xFFFFu, w.x >> 16, w.y & 0xFFFFu, w.y >> 16,
+                             w.z & 0xFFFFu, w.z >> 16, w.w & 0xFFFFu, w.w >> 16};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        a += v[j] <= m1 ? 1u : 0u;
+        b += v[j] <= m2 ? 1u : 0u;
+        c += v[j] <= m3 ? 1u : 0u;
+      }
+    }
+    *c1 = __reduce_add_sync(0xFFFFFFFFu, a);
+    *c2 = __reduce_add_sync(0xFFFFFFFFu, b);
+    *c3 = __reduce_add_sync(0xFFFFFFFFu, c);
+  };
+  if (lo >= 0xFFFFu) return 0xFFFFu;
+  uint32_t c1, c2, c3;
+  count_le(hi, hi, hi, &c1, &c2, &c3);
+  if (c1 < k) return 0xFFFFu;  // fewer than k numeric keys
+  // invariant: the answer lies in [lo, hi] and at least k keys are <= hi
+  while (lo < hi) {
+    const uint32_t m2 = (lo + hi) >> 1;
+    const uint32_t m1 = (lo + m2) >> 1;
+    const uint32_t m3 = (m2 + 1u + hi) >> 1;
+    count_le(m1, m2, m3, &c1, &c2, &c3);
+    if (c1 >= k) {
+      hi = m1;
+    } else if (c2 >= k) {
+      lo = m1 + 1u;
+      hi = m2;
+    } else if (c3 >= k) {
+      lo = m2 + 1u;
+      hi = m3;
+    } else {
+      lo = m3 + 1u;
+    }
+  }
+  return lo;
+}
+
 // k-th best group maximum of the chunk (descending key), or kNoThreshold when the chunk has
-// fewer than k non-NaN maxima.  One barrier: every warp then finds the k-th smallest of the
-// group keys itself, by binary search on the key value with warp-wide counts.
+// fewer than k non-NaN maxima.  Each maximum is a distinct element, so at least k elements
+// of the chunk are >= it and every member of the segment's top-k is >= it.  Two barriers:
+// the group keys go to shared memory, warp 0 selects, and the result is broadcast.
 template <bool BIG>
 __device__ uint32_t chunk_select(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
                                  Scratch<BIG>& sm) {
@@ -396,24 +469,14 @@ __device__ uint32_t chunk_select(const TopkParams& p, const StageInfo& si, const
   }
   for (int i = 0; i < nw; ++i) sm.gkeys[i * kThreads + tid] = kw[i];
   csync();
-  // lane l owns words [l * per, (l + 1) * per) of the nw * kThreads words
-  const int per = nw * kThreads / 32;
-  const uint32_t* src = sm.gkeys + lane * per;
-  uint32_t lo = 0, hi = 0xFFFFu;
-  const uint32_t k = static_cast<uint32_t>(p.k);
-  while (lo < hi) {
-    const uint32_t mid = (lo + hi) >> 1;
-    uint32_t cnt = 0;
-    for (int i = 0; i < per; i += 4) {
-      const uint4 w = lds128(src + i);
-      cnt += ((w.x & 0xFFFFu) <= mid) + ((w.x >> 16) <= mid) + ((w.y & 0xFFFFu) <= mid) +
-             ((w.y >> 16) <= mid) + ((w.z & 0xFFFFu) <= mid) + ((w.z >> 16) <= mid) +
-             ((w.w & 0xFFFFu) <= mid) + ((w.w >> 16) <= mid);
-    }
-    if (__reduce_add_sync(0xFFFFFFFFu, cnt) >= k) hi = mid; else lo = mid + 1;
+  if (tid < 32) {  // lane l owns words [l * per, (l + 1) * per) of the nw * kThreads words
+    const int per = nw * kThreads / 32;
+    const uint32_t K = kth_packed_keys(sm.gkeys + lane * per, per, static_cast<uint32_t>(p.k));
+    if (lane == 0) sm.bcast[3] = K;
+    if (lane == 0 && p.stats) atomicAdd(&p.status[3], 1u);
   }
-  if (tid == 0 && p.stats) atomicAdd(&p.status[3], 1u);
-  return lo;  // 0xFFFF: no certified threshold (fewer than k non-NaN maxima)
+  csync();
+  return sm.bcast[3];  // 0xFFFF: no certified threshold (fewer than k non-NaN maxima)
 }
 
 // Threshold test of one 16-byte vector: 8-bit element mask (bit e = element e) of values

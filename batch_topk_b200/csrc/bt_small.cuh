@@ -21,10 +21,11 @@ struct Counted {
 };
 
 // Counts this chunk's candidates under (K, STRICT) with one barrier and picks up the merger's
-// latest threshold for segment `seg` (uniform: staged through kuse[par] by thread 0).
+// latest threshold for segment `seg` (uniform: staged through kuse[par] by one thread).
+// Flips `par`: consecutive counts alternate between the two slot sets.
 template <bool STRICT>
 __device__ __forceinline__ Counted count_chunk(const StageInfo& si, const uint8_t* buf,
-                                               SmallScratch& sm, uint32_t K, int par, int seg) {
+                                               SmallScratch& sm, uint32_t K, int& par, int seg) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
@@ -62,6 +63,7 @@ __device__ __forceinline__ Counted count_chunk(const StageInfo& si, const uint8_
   c.total = total;
   c.base = wpre + incl - c.cnt;
   c.knext = sm.kuse[par];
+  par ^= 1;  // the next count uses the other slots: no barrier separates it from these reads
   return c;
 }
 
@@ -105,8 +107,8 @@ __device__ __forceinline__ void send_batch(SmallScratch& sm, int b, const BatchM
 
 // One non-empty chunk: threshold, count, write the batch, hand it to the merger.
 __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
-                           SmallScratch& sm, SegState& ss, int par, long long* nbp,
-                           uint32_t* guess) {
+                           SmallScratch& sm, SegState& ss, int& par, long long* nbp,
+                           uint32_t* guess, uint32_t* tight, bool* tight_hot) {
   const long long nb = *nbp;
   const uint32_t k = static_cast<uint32_t>(p.k);
   const uint32_t cap = static_cast<uint32_t>(p.cap);
@@ -117,7 +119,21 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
     c = count_chunk<true>(si, buf, sm, K, par, ss.s);
   } else {
     bool have = false;
-    if (ss.mycnt == 0 && *guess != kNoThreshold) {
+    if (ss.mycnt == 0 && *tight_hot && *tight != kNoThreshold && *tight != *guess) {
+      // the previous segment's final threshold: on tie-heavy rows it holds in this chunk
+      // already (>= k values at or beyond it), and then every later chunk is strict at it
+      c = count_chunk<false>(si, buf, sm, *tight, par, ss.s);
+      if (c.fail) return kChunkFail;
+      if (c.total >= k && c.total <= cap) {
+        K = *tight;
+        have = true;
+      } else {
+        *tight_hot = false;  // retried after one segment without it
+      }
+    } else if (ss.mycnt == 0) {
+      *tight_hot = true;
+    }
+    if (!have && ss.mycnt == 0 && *guess != kNoThreshold) {
       // the previous segment's first-chunk threshold, verified on this chunk: accepted when
       // it leaves between k and cap candidates here (then it is certified by this chunk)
       c = count_chunk<false>(si, buf, sm, *guess, par, ss.s);
@@ -158,7 +174,7 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
       uint64_t S;
       uint32_t sbase, stot;
       const uint32_t kstar = exact_local_select(p, si, buf, sm, K, strict, &S, &sbase, &stot);
-      if (!wait_batch_free(sm, nb)) return kChunkFail;
+      if (!wait_batch_free(sm, nb)) sm.fail = 1u;  // caught at the next barrier
       const int tid = threadIdx.x;
       const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf) + tid * 64;
       const long long e0 = si.cv0 * 8;
@@ -177,7 +193,7 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
   }
   const bool send = n > 0 || si.last;  // empty middle chunks need no hand-off
   if (!written && send) {
-    if (!wait_batch_free(sm, nb)) return kChunkFail;
+    if (!wait_batch_free(sm, nb)) sm.fail = 1u;  // caught at the next barrier
     if (c.flags) {
       if (strict) write_batch<true>(si, buf, c.flags, K, c.base, sm.batch[b]);
       else write_batch<false>(si, buf, c.flags, K, c.base, sm.batch[b]);
@@ -214,7 +230,9 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
                                     uint64_t* empty, const StageInfo* info, SmallScratch& sm) {
   constexpr int S = Cfg<false>::kStagesN;
   SegState ss;
-  uint32_t guess = kNoThreshold;
+  uint32_t guess = kNoThreshold;  // the previous part's first-chunk threshold
+  uint32_t tight = kNoThreshold;  // the previous part's final threshold
+  bool tight_hot = true;
   long long nb = 0;  // batches sent
   int st = 0, par = 0;
   uint32_t ph = 0;   // full-barrier phase parity of stage st
@@ -227,19 +245,51 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
     if (si.part == kStopPart) break;
     if (si.nvc > 0) {
       if (si.part != ss.part) {
+        tight = ss.K;
         ss = SegState{};
         ss.s = si.s;
         ss.part = si.part;
         ss.slot0 = si.slot;  // first slot of this part
       }
-      const int r = small_chunk(p, si, stages + static_cast<size_t>(st) * kStageBytes, sm, ss,
-                                par, &nb, &guess);
-      if (r == kChunkFail) {
-        failed = true;
-        break;
+      const uint8_t* buf = stages + static_cast<size_t>(st) * kStageBytes;
+      // Fast path for a middle chunk after a quiet one under a strict threshold: the max test
+      // and one OR-barrier; only when some value passes (or a wait failed) does the chunk go
+      // through the full count/compaction below.
+      // The chunk right after the part's first one is tried too: once the first chunk has
+      // certified a strict threshold, tie-heavy rows have nothing left to pass.
+      bool done = false;
+      if (ss.strict && ss.K < kNoThreshold && (ss.quiet || ss.mycnt == 1)) {
+        const uint32_t vb = key_to_bits(ss.K);
+        uint32_t cnt;
+        const uint32_t f = thread_flags<true>(si, buf, u32_as_h2(vb | (vb << 16)), false, &cnt);
+        done = !group_or<kThreads>(f != 0 || sm.fail != 0);
+        if (done) ss.quiet = true;
+        if (done && si.last) {  // nothing passed in the part's last chunk: the end marker
+          if (!wait_batch_free(sm, nb)) sm.fail = 1u;  // seen by all at the next barrier
+          BatchMeta meta;
+          meta.len = si.a1 - si.a0;
+          meta.part_slot = ss.slot0;
+          meta.seg_slot = si.slot - si.c;
+          meta.s = si.s;
+          meta.n = 0;
+          meta.flags = kBatchEnd;
+          meta.mycnt = ss.mycnt + 1;
+          meta.nchunks = si.nchunks;
+          meta.K = ss.K;
+          send_batch(sm, static_cast<int>(nb & 1), meta);
+          ++nb;
+        }
+      }
+      if (!done) {
+        const long long nb0 = nb;
+        const int r = small_chunk(p, si, buf, sm, ss, par, &nb, &guess, &tight, &tight_hot);
+        if (r == kChunkFail) {
+          failed = true;
+          break;
+        }
+        ss.quiet = nb == nb0;
       }
       ++ss.mycnt;
-      par ^= 1;
     }
     release_stage(&empty[st]);
     if (++st == S) {
