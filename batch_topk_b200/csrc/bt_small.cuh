@@ -493,14 +493,22 @@ __device__ void finalize_part(const TopkParams& p, const BatchMeta& m, unsigned 
   if (!last) return;
   __threadfence();
   int n = nl;
-  for (int c = 0; c < m.nchunks; ++c) {
-    const long long slot = m.seg_slot + c;
-    if (slot == m.part_slot) continue;  // this block's own part is already in L
-    int cnt = static_cast<int>(__ldcg(&p.chunk_count[slot]));
-    if (cnt <= 0) continue;
-    cnt = cnt < k ? cnt : k;  // a partial list holds at most k entries, ascending
-    absorb<R>(L, reinterpret_cast<const unsigned long long*>(p.cand + slot * p.cap), cnt, true);
-    n += cnt;
+  // the slot counts of the whole segment in one round trip (lanes in parallel); only each
+  // part's first slot holds a list
+  for (int c0 = 0; c0 < m.nchunks; c0 += 32) {
+    const long long slot = m.seg_slot + c0 + lane;
+    int cnt = 0;
+    if (c0 + lane < m.nchunks && slot != m.part_slot) {  // own part: already in L
+      cnt = static_cast<int>(__ldcg(&p.chunk_count[slot]));
+    }
+    for (unsigned todo = __ballot_sync(0xFFFFFFFFu, cnt > 0); todo; todo &= todo - 1) {
+      const int q = __ffs(todo) - 1;
+      int cq = __shfl_sync(0xFFFFFFFFu, cnt, q);
+      cq = cq < k ? cq : k;  // a partial list holds at most k entries, ascending
+      const long long sq = m.seg_slot + c0 + q;
+      absorb<R>(L, reinterpret_cast<const unsigned long long*>(p.cand + sq * p.cap), cq, true);
+      n += cq;
+    }
   }
   emit_row<R>(p, m.s, L, n < 32 * R ? n : 32 * R, m.len);
 }
