@@ -86,13 +86,16 @@ int g_tail_parts_env = -1;   // BT_TAIL_PARTS: parts per segment in the last wav
 int g_tail_segs_env = -1;    // BT_TAIL_SEGS: segments in the last wave (0: one per resident block)
 int g_grid_env = -1;         // BT_GRID: blocks of the streaming kernel (0: automatic)
 
-// Chunks per work part: about three parts per resident block, so blocks that run ahead take
-// more parts, while a part stays long enough to amortise its first-chunk threshold.
-int choose_part_chunks(long long total_chunks, long long resident) {
+// Chunks per work part.  With at least as many segments as resident blocks every block is
+// busy with whole segments, and a segment is never split: each extra part costs its own
+// first-chunk threshold and a cross-block merge of partial lists.  With fewer segments,
+// about one part per block.
+int choose_part_chunks(long long total_chunks, long long seg_num, long long resident) {
   if (g_part_chunks_env > 0) return g_part_chunks_env;
-  long long u = total_chunks / (3 * resident);
+  if (seg_num >= resident) return kMaxChunksPerSegment;
+  long long u = (total_chunks + resident - 1) / resident;
   if (u < 1) u = 1;
-  if (u > 64) u = 64;
+  if (u > kMaxChunksPerSegment) u = kMaxChunksPerSegment;
   return static_cast<int>(u);
 }
 
@@ -148,7 +151,7 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
   p.stats = g_stats > 0 ? 1 : 0;
   const bool big = p.k > Cfg<false>::kSelCap;
   const long long resident = static_cast<long long>(di.sms) * di.blocks_per_sm[big ? 1 : 0];
-  p.part_chunks = choose_part_chunks(work_items, resident);
+  p.part_chunks = choose_part_chunks(work_items, p.seg_num, resident);
   long long parts = work_items;  // CSR: an upper bound (every part holds a chunk)
   if (!csr) {
     const long long per = (p.p_max + p.part_chunks - 1) / p.part_chunks;

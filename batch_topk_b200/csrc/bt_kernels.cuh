@@ -132,6 +132,7 @@ struct alignas(16) Scratch {
   unsigned long long sel[Cfg<BIG>::kSelCap];
   alignas(16) uint32_t gkeys[Cfg<BIG>::kGroupWords * kThreads];  // 128-bit reads
   uint32_t coff[Cfg<BIG>::kCoffCap + 1];
+  uint32_t coff2[Cfg<BIG>::kCoffCap + 1];  // per-chunk offsets of the survivors of the merge filter
   uint32_t warp_tot[kWarps];
   alignas(16) uint32_t wcnt[2][kWarps];  // per-warp candidate counts, double-buffered
   int bin1, bin2;
@@ -628,6 +629,37 @@ __device__ __forceinline__ uint32_t buffer_kth_key(const Scratch<BIG>& sm, uint3
   return lo;
 }
 
+// Block-wide k-th smallest key among the n composites of the segment buffer: two 8-bit digit
+// histograms (aggregated shared atomics) instead of a per-warp search over the whole buffer.
+// kFewerThanK when n < k.  The histograms are zero on entry and left zero.
+template <bool BIG>
+__device__ uint32_t buffer_kth_key_block(Scratch<BIG>& sm, uint32_t n, uint32_t k) {
+  if (n < k) return kFewerThanK;
+  const int tid = threadIdx.x;
+  for (uint32_t i0 = 0; i0 < n; i0 += kThreads) {
+    const uint32_t i = i0 + tid;
+    const uint32_t key = i < n ? static_cast<uint32_t>(sm.cache[i] >> 48) : 0u;
+    hist_add_match(sm.hist1, key >> 8, i < n);
+  }
+  csync();
+  if (tid < 32) warp_find_bin(sm.hist1, 0, k, &sm.bin1, &sm.before1);
+  csync();
+  const uint32_t b1 = static_cast<uint32_t>(sm.bin1);
+  for (uint32_t i0 = 0; i0 < n; i0 += kThreads) {
+    const uint32_t i = i0 + tid;
+    const uint32_t key = i < n ? static_cast<uint32_t>(sm.cache[i] >> 48) : 0u;
+    hist_add_match(sm.hist2, key & 0xFFu, i < n && (key >> 8) == b1);
+  }
+  csync();
+  if (tid < 32) warp_find_bin(sm.hist2, sm.before1, k, &sm.bin2, &sm.before2);
+  csync();
+  const uint32_t kk = (b1 << 8) | static_cast<uint32_t>(sm.bin2);
+  sm.hist1[tid] = 0;
+  sm.hist2[tid] = 0;
+  csync();
+  return kk;
+}
+
 // Exact top-k selection among the chunk's candidates under threshold K (strict or not, or
 // take-all): the reference's two 8-bit digit passes plus ordered tie ranks.  Returns the
 // cutoff key; *S gets this thread's selected elements (bit 8*j+e), *sbase their first output
@@ -725,6 +757,32 @@ __device__ uint32_t exact_local(const TopkParams& p, const StageInfo& si, const 
 
 enum ChunkResult { kChunkDone = 0, kChunkOverflow = 1, kChunkFail = 2 };
 
+// Drops the segment buffer's composites with key > K, keeping their order; returns the new
+// count.  Each thread holds its kCacheCap / kThreads entries in registers across the scan's
+// barriers, so the in-place writes never overtake a read.
+template <bool BIG>
+__device__ uint32_t compact_cache(Scratch<BIG>& sm, uint32_t n, uint32_t K) {
+  constexpr int kPer = Cfg<BIG>::kCacheCap / kThreads;
+  const uint32_t i0 = threadIdx.x * kPer;
+  unsigned long long v[kPer];
+  uint32_t keep = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const uint32_t i = i0 + j;
+    v[j] = i < n ? sm.cache[i] : ~0ull;
+    keep += (i < n && static_cast<uint32_t>(v[j] >> 48) <= K) ? 1u : 0u;
+  }
+  uint32_t tot;
+  uint32_t w = block_excl_scan<kThreads, true>(keep, &tot, sm.warp_tot);
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const uint32_t i = i0 + j;
+    if (i < n && static_cast<uint32_t>(v[j] >> 48) <= K) sm.cache[w++] = v[j];
+  }
+  csync();
+  return tot;
+}
+
 // Counts the chunk's candidates under (ss.K, STRICT) with one barrier, then writes them in
 // index order.  `par` selects the double-buffered warp-count slots.
 template <bool STRICT, bool BIG>
@@ -763,7 +821,19 @@ __device__ int stream_chunk(const TopkParams& p, const StageInfo& si, const uint
   }
   if (total > static_cast<uint32_t>(p.cap)) return kChunkOverflow;
   const uint32_t base = wpre + incl - cnt;
-  const bool to_smem = !ss.spilled && ss.nbuf + total <= static_cast<uint32_t>(Cfg<BIG>::kCacheCap);
+  bool to_smem = !ss.spilled && ss.nbuf + total <= static_cast<uint32_t>(Cfg<BIG>::kCacheCap);
+  if (BIG && !to_smem && !ss.spilled && ss.nbuf >= static_cast<uint32_t>(p.k)) {
+    // make room: the buffer's k-th key is a tighter threshold (k composites at lower
+    // indices beat it), and the buffered composites beyond it can go
+    const uint32_t kk = buffer_kth_key_block(sm, ss.nbuf, static_cast<uint32_t>(p.k));
+    if (kk < ss.K) {
+      ss.K = kk;
+      ss.strict = true;
+    }
+    ss.nbuf = compact_cache<BIG>(sm, ss.nbuf, ss.K);
+    ss.added = 0;
+    to_smem = ss.nbuf + total <= static_cast<uint32_t>(Cfg<BIG>::kCacheCap);
+  }
   if (flags) write_flagged<STRICT, BIG>(p, si, buf, flags, v2, take_all, base, sm, ss.nbuf, to_smem);
   if (tid == 0) p.chunk_count[si.slot] = total;
   if (to_smem) {
@@ -779,7 +849,7 @@ __device__ int stream_chunk(const TopkParams& p, const StageInfo& si, const uint
     ss.strict = true;
     if (ss.added >= static_cast<uint32_t>(p.k) && !ss.spilled) {
       csync();
-      const uint32_t kk = buffer_kth_key(sm, ss.nbuf, static_cast<uint32_t>(p.k), ss.K);
+      const uint32_t kk = buffer_kth_key_block(sm, ss.nbuf, static_cast<uint32_t>(p.k));
       if (kk < ss.K) ss.K = kk;
       ss.added = 0;
     }
@@ -1036,6 +1106,63 @@ __device__ void merge_from_global(const TopkParams& p, const SegState& ss, uint3
   csync();
   const uint32_t n = sm.bcast[2];
   const long long len = ss.a1 - ss.a0;
+  if (small_p && n > static_cast<uint32_t>(C::kCacheCap)) {
+    // Too many candidates for the cache: keep only those with key <= kf (the segment's final
+    // threshold), in index order.  Pass 1 counts them per chunk, pass 2 compacts them, one
+    // warp per chunk with ballot ranks.  Usually they fit, and the cache merge runs.
+    const int warp = tid >> 5;
+    for (int c = warp; c < P; c += kWarps) {
+      const uint32_t cnt = sm.coff[c + 1] - sm.coff[c];
+      const uint32_t* src = p.cand + (ss.slot0 + c) * p.cap;
+      uint32_t keep = 0;
+      for (uint32_t i = lane; i < cnt; i += 32) keep += desc_key(__ldcg(src + i) >> 16) <= kf ? 1u : 0u;
+      keep = __reduce_add_sync(0xFFFFFFFFu, keep);
+      if (lane == 0) sm.coff2[c] = keep;
+    }
+    csync();
+    if (tid < 32) {
+      uint32_t carry = 0;
+      for (int base = 0; base < P; base += 32) {
+        const int c = base + lane;
+        const uint32_t v = c < P ? sm.coff2[c] : 0u;
+        uint32_t incl = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        if (c < P) sm.coff2[c] = carry + incl - v;
+        carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
+      }
+      if (lane == 0) sm.bcast[2] = carry;
+    }
+    csync();
+    const uint32_t nkeep = sm.bcast[2];
+    if (nkeep <= static_cast<uint32_t>(C::kCacheCap)) {
+      for (int c = warp; c < P; c += kWarps) {
+        const uint32_t cnt = sm.coff[c + 1] - sm.coff[c];
+        const uint32_t* src = p.cand + (ss.slot0 + c) * p.cap;
+        const long long e0 = (ss.v0 + static_cast<long long>(c) * ss.chunk_vecs) * 8;
+        uint32_t dst = sm.coff2[c];
+        for (uint32_t i0 = 0; i0 < cnt; i0 += 32) {
+          const uint32_t i = i0 + lane;
+          uint32_t w = 0;
+          bool keep = false;
+          if (i < cnt) {
+            w = __ldcg(src + i);
+            keep = desc_key(w >> 16) <= kf;
+          }
+          const unsigned b = __ballot_sync(0xFFFFFFFFu, keep);
+          if (keep) sm.cache[dst + __popc(b & ((1u << lane) - 1u))] = make_composite(w, e0, ss.a0);
+          dst += __popc(b);
+        }
+      }
+      csync();
+      emit_from_cache<BIG>(p, sm, nkeep, kf, ss.s, len);
+      return;
+    }
+    // still too many: the merge reads the chunk lists in place (below)
+  }
   if (small_p && n <= static_cast<uint32_t>(C::kCacheCap)) {
     const int warp = tid >> 5;
     for (int c = warp; c < P; c += kWarps) {
