@@ -36,11 +36,11 @@ long long csr_slot_bound(long long seg_num, long long total_len) {
 }
 
 struct Layout {
-  size_t status, thresh, done, chunk_start, part_start, counts, offs, cand, total;
+  size_t status, thresh, done, next, chunk_start, part_start, counts, offs, cand, total;
 };
 
-// status | seg_thresh | seg_done | chunk_start (CSR) | chunk_count | chunk_off | candidates,
-// each region 256-byte aligned.
+// status | seg_thresh | seg_done | chunk_next (fixed-length) | chunk_start, part_start (CSR) |
+// chunk_count | chunk_off | candidates, each region 256-byte aligned.
 Layout make_layout(long long seg_num, long long slots, int cap, bool csr) {
   Layout L{};
   size_t off = 0;
@@ -52,6 +52,7 @@ Layout make_layout(long long seg_num, long long slots, int cap, bool csr) {
   L.status = take(16 * sizeof(uint32_t));
   L.thresh = take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
   L.done = take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
+  L.next = csr ? 0 : take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
   L.chunk_start = csr ? take(static_cast<size_t>(seg_num + 1) * sizeof(uint32_t)) : 0;
   L.part_start = csr ? take(static_cast<size_t>(seg_num + 1) * sizeof(uint32_t)) : 0;
   L.counts = take(static_cast<size_t>(slots) * sizeof(uint32_t));
@@ -85,6 +86,7 @@ int g_part_chunks_env = -1;  // BT_PART_CHUNKS override of the work-part size (0
 int g_tail_parts_env = -1;   // BT_TAIL_PARTS: parts per segment in the last wave (0: off)
 int g_tail_segs_env = -1;    // BT_TAIL_SEGS: segments in the last wave (0: one per resident block)
 int g_grid_env = -1;         // BT_GRID: blocks of the streaming kernel (0: automatic)
+int g_steal_env = -1;        // BT_STEAL: 0 turns helping off
 
 // Chunks per work part.  With at least as many segments as resident blocks every block is
 // busy with whole segments, and a segment is never split: each extra part costs its own
@@ -137,6 +139,8 @@ cudaError_t device_info(DeviceInfo* out) {
       g_tail_segs_env = s ? std::atoi(s) : 0;
       s = std::getenv("BT_GRID");
       g_grid_env = s ? std::atoi(s) : 0;
+      s = std::getenv("BT_STEAL");
+      g_steal_env = s ? std::atoi(s) : 1;
     }
     d.ready = true;
   }
@@ -167,6 +171,10 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
     p.parts_total = static_cast<long long>(p.tail_seg0) * per +
                     static_cast<long long>(p.seg_num - p.tail_seg0) * p.tail_parts;
     parts = p.parts_total;
+    // Whole segments: claim chunk by chunk and let blocks that run dry help (BT_STEAL=0: off).
+    // Only for k <= 128, whose first chunk of a visit is cheap; for larger k a helper's first
+    // chunk (select plus exact select) costs more than the chunks it takes over.
+    p.steal = (!big && per == 1 && p.tail_seg0 == p.seg_num && g_steal_env != 0) ? 1 : 0;
   }
   if (csr) {
     csr_prep_kernel<<<1, 1024, 0, stream>>>(p);
@@ -179,6 +187,7 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
   long long grid_ll = parts < resident ? (parts > 0 ? parts : 1) : resident;
   if (g_grid_env > 0 && g_grid_env < grid_ll) grid_ll = g_grid_env;
   const int grid = static_cast<int>(grid_ll);
+  p.help_window = p.steal ? (grid < p.seg_num ? grid : p.seg_num) : 0;
   if (g_prof_start) cudaEventRecord(g_prof_start, stream);
   if (big) {
     topk_kernel<true><<<grid, block_threads<true>(), SmemLayout<true>::bytes, stream>>>(p);
@@ -206,6 +215,7 @@ TopkParams base_params(const void* d_input, int seg_num, int k, void* d_out_valu
   p.status = reinterpret_cast<uint32_t*>(ws + L.status);
   p.seg_thresh = reinterpret_cast<uint32_t*>(ws + L.thresh);
   p.seg_done = reinterpret_cast<uint32_t*>(ws + L.done);
+  p.chunk_next = reinterpret_cast<uint32_t*>(ws + L.next);
   p.chunk_start = reinterpret_cast<uint32_t*>(ws + L.chunk_start);
   p.part_start = reinterpret_cast<uint32_t*>(ws + L.part_start);
   p.chunk_count = reinterpret_cast<uint32_t*>(ws + L.counts);

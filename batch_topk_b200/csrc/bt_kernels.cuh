@@ -56,6 +56,9 @@ struct TopkParams {
   int part_chunks;               // at most this many chunks per work part
   int tail_seg0;                 // fixed-length: segments from here on are cut into
   int tail_parts;                //   tail_parts parts each (the last wave ends evenly)
+  int steal;                     // whole segments, chunks claimed one by one, idle blocks help
+  int help_window;               // how many of the last-claimed segments idle blocks may help
+  uint32_t* chunk_next;          // [seg_num] next unclaimed chunk of each segment (steal)
   int k;
   int groups;                    // group maxima per thread in the threshold select
   int cap;                       // candidate capacity per chunk slot
@@ -123,6 +126,8 @@ struct StageInfo {
 };
 constexpr int kStopPart = -1;
 constexpr uint32_t kWorkCounter = 8;  // status[8]: next work part to claim (reset per call)
+constexpr uint32_t kHelpCounter = 9;  // status[9]: next segment an idle block helps
+constexpr int kHelpMinChunks = 3;     // a helper joins a segment with at least this many left
 
 template <bool BIG>
 struct alignas(16) Scratch {
@@ -280,35 +285,72 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
     }
     return true;
   };
-  long long part = atomicAdd(&p.status[kWorkCounter], 1u);
-  while (ok && part < nparts) {
-    const long long next = atomicAdd(&p.status[kWorkCounter], 1u);  // claim ahead
-    int s, c0, c1;
-    SegGeom g;
-    long long slot0;
-    decode_part(p, part, &s, &c0, &c1, &g, &slot0);
-    for (int c = c0; c < c1 && ok; ++c) {
-      StageInfo si;
-      si.s = s;
-      si.c = c;
-      si.part = static_cast<int>(part);
-      si.slot = slot0 + c;
-      si.a0 = g.a0;
-      si.a1 = g.a1;
-      si.v0 = g.v0;
-      si.nchunks = g.nchunks;
-      si.chunk_vecs = g.chunk_vecs;
-      si.last = c == c1 - 1 ? 1 : 0;
-      si.cv0 = g.v0 + static_cast<long long>(c) * g.chunk_vecs;
-      const long long rem = g.v0 + g.nv - si.cv0;
-      si.nvc = static_cast<int>(rem < g.chunk_vecs ? rem : g.chunk_vecs);
-      const long long first = g.v0 - si.cv0;
-      const long long last = ((g.a1 - 1) >> 3) - si.cv0;
-      si.vlo = ((g.a0 & 7) && first >= 0 && first < si.nvc) ? static_cast<int>(first) : -1;
-      si.vhi = ((g.a1 & 7) && last >= 0 && last < si.nvc) ? static_cast<int>(last) : -1;
-      ok = put(si);
+  // chunk c of segment s (geometry g, chunk slots from slot0) as work part `part`
+  auto chunk_info = [&](int s, const SegGeom& g, long long slot0, int c, int part, bool last_c) {
+    StageInfo si;
+    si.s = s;
+    si.c = c;
+    si.part = part;
+    si.slot = slot0 + c;
+    si.a0 = g.a0;
+    si.a1 = g.a1;
+    si.v0 = g.v0;
+    si.nchunks = g.nchunks;
+    si.chunk_vecs = g.chunk_vecs;
+    si.last = last_c ? 1 : 0;
+    si.cv0 = g.v0 + static_cast<long long>(c) * g.chunk_vecs;
+    const long long rem = g.v0 + g.nv - si.cv0;
+    si.nvc = static_cast<int>(rem < g.chunk_vecs ? rem : g.chunk_vecs);
+    const long long first = g.v0 - si.cv0;
+    const long long last = ((g.a1 - 1) >> 3) - si.cv0;
+    si.vlo = ((g.a0 & 7) && first >= 0 && first < si.nvc) ? static_cast<int>(first) : -1;
+    si.vhi = ((g.a1 & 7) && last >= 0 && last < si.nvc) ? static_cast<int>(last) : -1;
+    return si;
+  };
+  if (p.steal) {
+    // Whole segments, claimed in order.  A segment's chunks are claimed one at a time (one
+    // ahead, so the claim's latency hides behind the stage wait).  Once every segment is
+    // claimed, a block that has run dry helps one of the segments claimed last: it takes
+    // the chunks the owner has not claimed yet, and the split-segment merge joins the two
+    // lists.  Each visit of a block to a segment is one work part (numbered per block).
+    int visit = 0;
+    long long s = atomicAdd(&p.status[kWorkCounter], 1u);
+    bool own = true;
+    while (ok) {
+      if (s >= p.seg_num) {
+        own = false;
+        const long long h = atomicAdd(&p.status[kHelpCounter], 1u);
+        if (h >= p.help_window) break;
+        s = p.seg_num - 1 - h;
+      }
+      const SegGeom g = seg_geom(p, static_cast<int>(s));
+      const long long slot0 = s * p.p_max;
+      if (!own && static_cast<int>(__ldcg(&p.chunk_next[s])) + kHelpMinChunks > g.nchunks) {
+        s = p.seg_num;  // too little left to repay a helper's first chunk: try the next one
+        continue;
+      }
+      int c = static_cast<int>(atomicAdd(&p.chunk_next[s], 1u));
+      while (ok && c < g.nchunks) {
+        const int cn = static_cast<int>(atomicAdd(&p.chunk_next[s], 1u));
+        ok = put(chunk_info(static_cast<int>(s), g, slot0, c, visit, cn >= g.nchunks));
+        c = cn;
+      }
+      ++visit;
+      s = own ? static_cast<long long>(atomicAdd(&p.status[kWorkCounter], 1u)) : p.seg_num;
     }
-    part = next;
+  } else {
+    long long part = atomicAdd(&p.status[kWorkCounter], 1u);
+    while (ok && part < nparts) {
+      const long long next = atomicAdd(&p.status[kWorkCounter], 1u);  // claim ahead
+      int s, c0, c1;
+      SegGeom g;
+      long long slot0;
+      decode_part(p, part, &s, &c0, &c1, &g, &slot0);
+      for (int c = c0; c < c1 && ok; ++c) {
+        ok = put(chunk_info(s, g, slot0, c, static_cast<int>(part), c == c1 - 1));
+      }
+      part = next;
+    }
   }
   if (ok) {  // the stop sentinel
     StageInfo z{};
@@ -1336,11 +1378,15 @@ topk_kernel(TopkParams p) {
 // Fixed-length rows: reset the per-segment thresholds, arrival counters and status words.
 __global__ void init_kernel(TopkParams p) {
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   if (i < 16) p.status[i] = 0;
-  for (long long s = i; s < p.seg_num; s += static_cast<long long>(gridDim.x) * blockDim.x) {
+  for (long long s = i; s < p.seg_num; s += stride) {
     p.seg_thresh[s] = kNoThreshold;
     p.seg_done[s] = 0;
+    if (p.steal) p.chunk_next[s] = 0;
   }
+  // a split segment's partial lists are found by their non-zero slot count
+  for (long long c = i; c < p.slot_capacity; c += stride) p.chunk_count[c] = 0;
 }
 
 // CSR batches: the same resets, the chunk-slot prefix over segments, and the padding rows of
@@ -1349,6 +1395,7 @@ __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
   __shared__ uint32_t warp_tot[32];
   const int tid = threadIdx.x;
   if (tid < 16) p.status[tid] = 0;
+  for (long long c = tid; c < p.slot_capacity; c += 1024) p.chunk_count[c] = 0;
   __syncthreads();
   uint32_t carry = 0, pcarry = 0;
   for (int base = 0; base < p.seg_num; base += 1024) {

@@ -477,9 +477,9 @@ __device__ void finalize_part(const TopkParams& p, const BatchMeta& m, unsigned 
     const int pos = (r << 5) + lane;
     if (pos < np) dst[pos] = L[r];
   }
-  for (int c = lane; c < m.mycnt; c += 32) {
-    p.chunk_count[m.part_slot + c] = c == 0 ? static_cast<uint32_t>(np) : 0u;
-  }
+  // only the part's first slot carries a count (every slot count starts at zero per call:
+  // a part's chunks need not be contiguous when idle blocks help)
+  if (lane == 0) p.chunk_count[m.part_slot] = static_cast<uint32_t>(np);
   __threadfence();
   __syncwarp();
   int last = 0;
