@@ -148,6 +148,23 @@ cudaError_t device_info(DeviceInfo* out) {
   return cudaSuccess;
 }
 
+// The streaming kernel with programmatic stream serialisation: its prologue overlaps the
+// set-up kernel, which it waits for (grid_dep_wait) before touching the workspace.
+template <bool BIG>
+cudaError_t launch_topk(const TopkParams& p, int grid, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(block_threads<BIG>()));
+  cfg.dynamicSmemBytes = SmemLayout<BIG>::bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, topk_kernel<BIG>, p);
+}
+
 cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaStream_t stream) {
   DeviceInfo di;
   cudaError_t e = device_info(&di);
@@ -189,12 +206,7 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
   const int grid = static_cast<int>(grid_ll);
   p.help_window = p.steal ? (grid < p.seg_num ? grid : p.seg_num) : 0;
   if (g_prof_start) cudaEventRecord(g_prof_start, stream);
-  if (big) {
-    topk_kernel<true><<<grid, block_threads<true>(), SmemLayout<true>::bytes, stream>>>(p);
-  } else {
-    topk_kernel<false><<<grid, block_threads<false>(), SmemLayout<false>::bytes, stream>>>(p);
-  }
-  e = cudaGetLastError();
+  e = big ? launch_topk<true>(p, grid, stream) : launch_topk<false>(p, grid, stream);
   if (e != cudaSuccess) return e;
   if (g_prof_stop) cudaEventRecord(g_prof_stop, stream);
   return cudaSuccess;

@@ -171,6 +171,17 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialisation may
+// start while the previous kernel in the stream still runs; grid_dep_wait() returns once that
+// kernel has completed and its memory is visible (a no-op without such a launch).
+// grid_dep_launch() lets the next kernel start early.
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint4 lds128(const void* p) {
   return *reinterpret_cast<const uint4*>(p);
 }

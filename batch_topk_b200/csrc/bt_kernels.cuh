@@ -1358,6 +1358,7 @@ topk_kernel(TopkParams p) {
     sm.hist2[tid] = 0;
   }
   __syncthreads();
+  grid_dep_wait();  // the set-up kernel's resets are complete and visible from here on
   if (tid >= kThreads) {
     if (tid == kThreads) {
       producer_loop<BIG>(p, stages, full, empty, info);
@@ -1377,6 +1378,7 @@ topk_kernel(TopkParams p) {
 
 // Fixed-length rows: reset the per-segment thresholds, arrival counters and status words.
 __global__ void init_kernel(TopkParams p) {
+  grid_dep_launch();  // the streaming kernel may set up meanwhile; it waits before any use
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   if (i < 16) p.status[i] = 0;
@@ -1393,6 +1395,7 @@ __global__ void init_kernel(TopkParams p) {
 // empty segments (which no chunk work item covers).  One block.
 __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
   __shared__ uint32_t warp_tot[32];
+  grid_dep_launch();  // the streaming kernel may set up meanwhile; it waits before any use
   const int tid = threadIdx.x;
   if (tid < 16) p.status[tid] = 0;
   for (long long c = tid; c < p.slot_capacity; c += 1024) p.chunk_count[c] = 0;
