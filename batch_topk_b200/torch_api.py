@@ -130,3 +130,32 @@ def topk_from_host(x_host: torch.Tensor, k: int, *, out_host: tuple | None = Non
         hi.copy_(idx, non_blocking=True)
     s.synchronize()
     return hv, hi
+
+
+# ---- PyTorch operator registration ---------------------------------------------------------
+#
+# torch.ops.batch_topk_b200.topk(x, k) and .topk_segmented(x, offsets, k): the same calls as
+# topk / topk_segmented, registered as custom operators with fake (shape-only) kernels, so they
+# trace under torch.compile and torch.export.  Each launch runs on the current stream.
+
+@torch.library.custom_op("batch_topk_b200::topk", mutates_args=())
+def _topk_op(x: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    return topk(x, k)
+
+
+@_topk_op.register_fake
+def _topk_op_fake(x: torch.Tensor, k: int):
+    if x.dim() != 2 or x.dtype != torch.float16:
+        raise ValueError("x must be a 2-D float16 tensor")
+    return (x.new_empty((x.shape[0], k)), x.new_empty((x.shape[0], k), dtype=torch.int32))
+
+
+@torch.library.custom_op("batch_topk_b200::topk_segmented", mutates_args=())
+def _topk_segmented_op(x: torch.Tensor, offsets: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    return topk_segmented(x, offsets, k)
+
+
+@_topk_segmented_op.register_fake
+def _topk_segmented_op_fake(x: torch.Tensor, offsets: torch.Tensor, k: int):
+    n = offsets.shape[0] - 1
+    return (x.new_empty((n, k)), x.new_empty((n, k), dtype=torch.int32))

@@ -1,0 +1,76 @@
+"""torch.ops.batch_topk_b200.{topk, topk_segmented}: the custom-operator registration over the
+C ABI.  The fake (shape-only) kernels are checked on the CPU; the GPU tests compare the
+operator with the oracle (bit-exact), with torch.topk (values), and under torch.compile."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import batch_topk_b200.torch_api  # noqa: F401  (registers the operators)
+from batch_topk_b200 import workloads as wl
+from util import assert_exact
+
+
+def test_fake_kernels_give_shapes():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        x = torch.empty((7, 1000), dtype=torch.float16, device="cuda")
+        v, i = torch.ops.batch_topk_b200.topk(x, 13)
+        assert v.shape == (7, 13) and v.dtype == torch.float16
+        assert i.shape == (7, 13) and i.dtype == torch.int32
+        off = torch.empty((9,), dtype=torch.int32, device="cuda")
+        x1 = torch.empty((5000,), dtype=torch.float16, device="cuda")
+        v, i = torch.ops.batch_topk_b200.topk_segmented(x1, off, 4)
+        assert v.shape == (8, 4) and i.shape == (8, 4)
+
+
+def test_fake_kernel_rejects_wrong_dtype():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode(), pytest.raises(ValueError):
+        torch.ops.batch_topk_b200.topk(torch.empty((2, 10), dtype=torch.float32, device="cuda"), 3)
+
+
+@pytest.mark.gpu
+def test_operator_matches_oracle_and_torch_topk(orc):
+    x = wl.gen_c2(rows=slice(0, 16))
+    xt = torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16)
+    v, i = torch.ops.batch_topk_b200.topk(xt, 50)
+    exp_v, exp_i = orc.topk(x, 50)
+    assert_exact(v.cpu().view(torch.int16).numpy().view(np.uint16), i.cpu().numpy(), exp_v, exp_i,
+                 "op vs oracle")
+    tv, _ = torch.topk(xt, 50, dim=1)  # values agree; torch's order among ties is unspecified
+    assert torch.equal(v, tv)
+    assert torch.equal(torch.gather(xt, 1, i.long()), v)
+
+
+@pytest.mark.gpu
+def test_operator_under_torch_compile(orc):
+    x = wl.gen_c1()
+    xt = torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16)
+
+    def f(t):
+        v, i = torch.ops.batch_topk_b200.topk(t * 2, 50)
+        return v.float().sum(dim=1), i
+
+    g = torch.compile(f, fullgraph=True)
+    s_ref, i_ref = f(xt)
+    s_cmp, i_cmp = g(xt)
+    assert torch.equal(i_ref, i_cmp) and torch.equal(s_ref, s_cmp)
+
+
+@pytest.mark.gpu
+def test_segmented_operator(orc):
+    rng = np.random.default_rng(3)
+    lens = np.array([0, 5, 100, 20000, 7, 70000])
+    off = np.zeros(lens.size + 1, np.int64)
+    np.cumsum(lens, out=off[1:])
+    vals = rng.standard_normal(int(off[-1])).astype(np.float16).view(np.uint16)
+    xt = torch.from_numpy(vals.view(np.int16)).cuda().view(torch.float16)
+    ot = torch.from_numpy(off.astype(np.int32)).cuda()
+    v, i = torch.ops.batch_topk_b200.topk_segmented(xt, ot, 50)
+    exp_v, exp_i = orc.topk_csr(vals, off, 50)
+    assert_exact(v.cpu().view(torch.int16).numpy().view(np.uint16), i.cpu().numpy(), exp_v, exp_i,
+                 "segmented op vs oracle")
