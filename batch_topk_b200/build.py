@@ -13,8 +13,10 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 SRC = os.path.join(HERE, "csrc", "batch_topk.cu")
+GEN_SRC = os.path.join(HERE, "csrc", "gen.cu")  # device-side input generation
 HEADERS = [os.path.join(HERE, "csrc", f) for f in ("bt_device.cuh", "bt_kernels.cuh", "bt_small.cuh")] + [
-    os.path.join(REPO, "include", "batch_topk_b200.h")
+    os.path.join(REPO, "include", "batch_topk_b200.h"),
+    os.path.join(REPO, "include", "batch_topk_b200_gen.h"),
 ]
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libbatch_topk_b200.so")
@@ -37,7 +39,7 @@ def up_to_date() -> bool:
     if not os.path.exists(LIB):
         return False
     t = os.path.getmtime(LIB)
-    return all(os.path.getmtime(p) <= t for p in [SRC, *HEADERS])
+    return all(os.path.getmtime(p) <= t for p in [SRC, GEN_SRC, *HEADERS])
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
@@ -45,7 +47,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return LIB
     os.makedirs(LIB_DIR, exist_ok=True)
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-o", tmp, SRC]
+    cmd = [nvcc(), *NVCC_FLAGS, "-o", tmp, SRC, GEN_SRC]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -147,6 +147,15 @@ def gen_c1(rows=None, seg_len=None, seed=None) -> np.ndarray:
     return to_half_bits(normal(seed or cfg.seed, 0, idx)).reshape(r.size, L)
 
 
+def c2_outliers(row: int, seg_len: int, seed: int):
+    """C2's 20 planted outliers of one row: (distinct positions, fp16 bits of U(8,12))."""
+    cand = (rand_u64(seed, 2, row * 64 + np.arange(64, dtype=np.int64)) % np.uint64(seg_len)).astype(np.int64)
+    _, first = np.unique(cand, return_index=True)
+    pos = cand[np.sort(first)][:20]  # the first 20 distinct draws, in draw order
+    assert pos.size == 20
+    return pos, uniform_half(seed, 3, row * 64 + np.arange(20, dtype=np.int64), 8.0, 12.0)
+
+
 def gen_c2(rows=None, seg_len=None, seed=None) -> np.ndarray:
     cfg = CONFIGS["C2"]
     L = seg_len or cfg.seg_len
@@ -159,12 +168,8 @@ def gen_c2(rows=None, seg_len=None, seed=None) -> np.ndarray:
         v = to_half_bits(normal(s, 0, idx, sigma=2.0))
         masked = uniform01(rand_u64(s, 1, idx)) < 0.05
         v[masked] = 0xFC00
-        # 20 distinct positions: first 20 unique of a per-row draw sequence
-        cand = (rand_u64(s, 2, row * 64 + np.arange(64, dtype=np.int64)) % np.uint64(L)).astype(np.int64)
-        _, first = np.unique(cand, return_index=True)
-        pos = cand[np.sort(first)][:20]
-        assert pos.size == 20
-        v[pos] = uniform_half(s, 3, row * 64 + np.arange(20, dtype=np.int64), 8.0, 12.0)
+        pos, vals = c2_outliers(int(row), L, s)
+        v[pos] = vals
         out[j] = v
     return out
 
