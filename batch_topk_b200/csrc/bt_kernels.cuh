@@ -138,6 +138,8 @@ struct alignas(16) Scratch {
   alignas(16) uint32_t gkeys[Cfg<BIG>::kGroupWords * kThreads];  // 128-bit reads
   uint32_t coff[Cfg<BIG>::kCoffCap + 1];
   uint32_t coff2[Cfg<BIG>::kCoffCap + 1];  // per-chunk offsets of the survivors of the merge filter
+  unsigned long long tmask[kThreads];      // balanced write: each thread's candidate bits
+  uint32_t tbase[kThreads];                // balanced write: each thread's first output slot
   uint32_t warp_tot[kWarps];
   alignas(16) uint32_t wcnt[2][kWarps];  // per-warp candidate counts, double-buffered
   int bin1, bin2;
@@ -386,6 +388,7 @@ struct SegState {
   uint32_t nbuf = 0;          // candidates of this segment in sm.cache
   uint32_t added = 0;         // candidates added since the threshold was last tightened
   bool quiet = false;         // the previous chunk of the part sent nothing
+  bool rising = false;        // the previous chunk overflowed its threshold (large k)
   long long slot0 = 0, v0 = 0, a0 = 0, a1 = 0;
 };
 
@@ -825,6 +828,62 @@ __device__ uint32_t compact_cache(Scratch<BIG>& sm, uint32_t n, uint32_t K) {
   return tot;
 }
 
+// Position of the r-th set bit (r from 0) of a 64-bit mask.
+__device__ __forceinline__ int select_bit64(unsigned long long m, uint32_t r) {
+  const uint32_t lo = static_cast<uint32_t>(m);
+  const uint32_t pl = static_cast<uint32_t>(__popc(lo));
+  uint32_t w = r < pl ? lo : static_cast<uint32_t>(m >> 32);
+  uint32_t rr = r < pl ? r : r - pl;
+  int pos = r < pl ? 0 : 32;
+#pragma unroll
+  for (int width = 16; width >= 1; width >>= 1) {
+    const uint32_t c = static_cast<uint32_t>(__popc(w & ((1u << width) - 1u)));
+    if (rr >= c) {
+      rr -= c;
+      w >>= width;
+      pos += width;
+    }
+  }
+  return pos;
+}
+
+// Writes the chunk's `total` candidates in index order like write_flagged, but spread over the
+// block: every thread takes output slots tid, tid + kThreads, ... and finds each one's owner
+// thread (binary search over the prefixes) and element (the rank-th set bit of the owner's
+// mask).  For clustered candidates (a sorted row's top values sit in a few threads) this keeps
+// the block from waiting on a few serial writers.
+template <bool STRICT, bool BIG>
+__device__ void write_balanced(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
+                               uint32_t flags, __half2 v2, bool take_all, uint32_t base,
+                               uint32_t total, Scratch<BIG>& sm, uint32_t nbuf, bool to_smem) {
+  const int tid = threadIdx.x;
+  unsigned long long M = 0;
+  for (uint32_t f = flags; f; f &= f - 1) {
+    const int j = __ffs(f) - 1;
+    M |= static_cast<unsigned long long>(vec_mask<STRICT>(si, buf, tid * kVecPerThread + j, v2,
+                                                          take_all)) << (8 * j);
+  }
+  sm.tmask[tid] = M;
+  sm.tbase[tid] = base;
+  csync();
+  uint32_t* out = p.cand + si.slot * p.cap;
+  const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf);
+  const long long e0 = si.cv0 * 8;
+  for (uint32_t i = tid; i < total; i += kThreads) {
+    int lo = 0, hi = kThreads - 1;  // owner: the last thread whose first slot is <= i
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (sm.tbase[mid] <= i) lo = mid; else hi = mid - 1;
+    }
+    const int pos = select_bit64(sm.tmask[lo], i - sm.tbase[lo]);
+    const uint32_t lidx = static_cast<uint32_t>(lo * 64 + pos);
+    const uint32_t w = (static_cast<uint32_t>(v16[lidx]) << 16) | lidx;
+    out[i] = w;
+    if (to_smem) sm.cache[nbuf + i] = make_composite(w, e0, si.a0);
+  }
+  csync();  // tmask / tbase are free again
+}
+
 // Counts the chunk's candidates under (ss.K, STRICT) with one barrier, then writes them in
 // index order.  `par` selects the double-buffered warp-count slots.
 template <bool STRICT, bool BIG>
@@ -876,7 +935,11 @@ __device__ int stream_chunk(const TopkParams& p, const StageInfo& si, const uint
     ss.added = 0;
     to_smem = ss.nbuf + total <= static_cast<uint32_t>(Cfg<BIG>::kCacheCap);
   }
-  if (flags) write_flagged<STRICT, BIG>(p, si, buf, flags, v2, take_all, base, sm, ss.nbuf, to_smem);
+  if (BIG && total >= 512) {
+    write_balanced<STRICT, BIG>(p, si, buf, flags, v2, take_all, base, total, sm, ss.nbuf, to_smem);
+  } else if (flags) {
+    write_flagged<STRICT, BIG>(p, si, buf, flags, v2, take_all, base, sm, ss.nbuf, to_smem);
+  }
   if (tid == 0) p.chunk_count[si.slot] = total;
   if (to_smem) {
     ss.nbuf += total;
@@ -889,6 +952,8 @@ __device__ int stream_chunk(const TopkParams& p, const StageInfo& si, const uint
     // exact pass, earlier in index order): later chunks only need key < K.  Once k more
     // candidates have arrived, tighten K to the exact k-th best of the buffer.
     ss.strict = true;
+    // once k more candidates have arrived, tighten K to the buffer's k-th key (k composites at
+    // lower indices beat it, so it is a strict threshold)
     if (ss.added >= static_cast<uint32_t>(p.k) && !ss.spilled) {
       csync();
       const uint32_t kk = buffer_kth_key_block(sm, ss.nbuf, static_cast<uint32_t>(p.k));
@@ -903,8 +968,9 @@ __device__ int stream_chunk(const TopkParams& p, const StageInfo& si, const uint
 // and fall back to the exact local select when too many values pass.
 template <bool BIG>
 __device__ int first_chunk(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
-                           Scratch<BIG>& sm, SegState& ss, int par) {
+                           Scratch<BIG>& sm, SegState& ss, int par, bool* adopted = nullptr) {
   const uint32_t kc = chunk_select(p, si, buf, sm);
+  if (adopted) *adopted = kc < ss.K;
   if (kc < ss.K) {
     ss.K = kc;
     ss.strict = false;
@@ -1275,9 +1341,20 @@ __device__ void consumer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
     const uint8_t* buf = stages + static_cast<size_t>(st) * kStageBytes;
     int r = kChunkDone;
     if (si.part == ss.part && ss.strict && si.nvc > 0) {  // uniform: stage info is shared
-      // steady state: one barrier per chunk, usually nothing to write
-      r = stream_chunk<true, BIG>(p, si, buf, sm, ss, par);
-      if (r == kChunkOverflow) r = first_chunk<BIG>(p, si, buf, sm, ss, par);  // values ramped up
+      // steady state: one barrier per chunk, usually nothing to write.  After an overflow
+      // (values rising along the row) the next chunk starts from its own threshold instead
+      // of counting everything under the stale one first.
+      if (ss.rising) {
+        bool adopted;
+        r = first_chunk<BIG>(p, si, buf, sm, ss, par, &adopted);
+        ss.rising = adopted;  // still rising while the chunk's own threshold beats the old one
+      } else {
+        r = stream_chunk<true, BIG>(p, si, buf, sm, ss, par);
+        if (r == kChunkOverflow) {
+          r = first_chunk<BIG>(p, si, buf, sm, ss, par);  // values ramped up
+          ss.rising = true;
+        }
+      }
     } else {
       if (group_or<kThreads>(!ok)) r = kChunkFail;
       if (r != kChunkFail) {
