@@ -145,6 +145,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking query of the same phase (acquire semantics as for try_wait): issued early, its
+// latency overlaps other work, and a phase found complete needs no wait later.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: returns false if the phase did not complete within kWaitCap tries (each
 // try suspends for at most kWaitHintNs, so the bound is about a second).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {

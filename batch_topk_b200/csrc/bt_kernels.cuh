@@ -392,13 +392,6 @@ struct SegState {
   long long slot0 = 0, v0 = 0, a0 = 0, a1 = 0;
 };
 
-__device__ __forceinline__ uint4 masked_vec(const StageInfo& si, const uint8_t* buf, int vi,
-                                            bool* partial, uint32_t* valid) {
-  const uint4 w = lds128(buf + vi * 16);
-  *partial = (vi == si.vlo) || (vi == si.vhi);
-  *valid = *partial ? valid_mask8(si.cv0 + vi, si.a0, si.a1) : 0xFFu;
-  return w;
-}
 
 // k-th smallest of the packed 16-bit keys a warp holds at src (words [lane * per, +per) per
 // lane; 0xFFFF keys are NaN maxima or padding), or 0xFFFF when fewer than k keys are
@@ -461,6 +454,59 @@ __device__ __forceinline__ uint32_t kth_packed_keys(const uint32_t* src, int per
   return lo;
 }
 
+// kth_packed_keys for 16 keys a lane (8 words at src), held in registers across the search
+// steps instead of re-read from shared memory at each step.
+__device__ __forceinline__ uint32_t kth_keys16(const uint32_t* src, uint32_t k) {
+  const uint4 wa = lds128(src), wb = lds128(src + 4);
+  const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+  uint32_t lo = 0xFFFFu, hi = 0u;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint32_t v = (w[j >> 1] >> ((j & 1) * 16)) & 0xFFFFu;
+    lo = v < lo ? v : lo;
+    hi = (v < 0xFFFFu && v > hi) ? v : hi;
+  }
+  lo = __reduce_min_sync(0xFFFFFFFFu, lo);
+  hi = __reduce_max_sync(0xFFFFFFFFu, hi);
+  if (lo >= 0xFFFFu) return 0xFFFFu;
+  auto count3 = [&](uint32_t m1, uint32_t m2, uint32_t m3, uint32_t* c1, uint32_t* c2,
+                    uint32_t* c3) {
+    uint32_t a = 0, b = 0, c = 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t v = (w[j >> 1] >> ((j & 1) * 16)) & 0xFFFFu;
+      a += v <= m1 ? 1u : 0u;
+      b += v <= m2 ? 1u : 0u;
+      c += v <= m3 ? 1u : 0u;
+    }
+    *c1 = __reduce_add_sync(0xFFFFFFFFu, a);
+    *c2 = __reduce_add_sync(0xFFFFFFFFu, b);
+    *c3 = __reduce_add_sync(0xFFFFFFFFu, c);
+  };
+  uint32_t c1, c2, c3;
+  count3(hi, hi, hi, &c1, &c2, &c3);
+  if (c1 < k) return 0xFFFFu;  // fewer than k numeric keys
+  // invariant: the answer lies in [lo, hi] and at least k keys are <= hi
+  while (lo < hi) {
+    const uint32_t m2 = (lo + hi) >> 1;
+    const uint32_t m1 = (lo + m2) >> 1;
+    const uint32_t m3 = (m2 + 1u + hi) >> 1;
+    count3(m1, m2, m3, &c1, &c2, &c3);
+    if (c1 >= k) {
+      hi = m1;
+    } else if (c2 >= k) {
+      lo = m1 + 1u;
+      hi = m2;
+    } else if (c3 >= k) {
+      lo = m2 + 1u;
+      hi = m3;
+    } else {
+      lo = m3 + 1u;
+    }
+  }
+  return lo;
+}
+
 // k-th best group maximum of the chunk (descending key), or kNoThreshold when the chunk has
 // fewer than k non-NaN maxima.  Each maximum is a distinct element, so at least k elements
 // of the chunk are >= it and every member of the segment's top-k is >= it.  Two barriers:
@@ -471,14 +517,15 @@ __device__ uint32_t chunk_select(const TopkParams& p, const StageInfo& si, const
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   uint32_t acc0 = 0x7E007E00u, acc1 = 0x7E007E00u, acc2 = 0x7E007E00u, acc3 = 0x7E007E00u;
-#pragma unroll
+  const int nvc = si.nvc, vlo = si.vlo, vhi = si.vhi;
+  // Rolled: this pass runs once per segment, mostly with a cold instruction cache, where
+  // the unrolled form cost about twice as many cycles.
+#pragma unroll 1
   for (int j = 0; j < kVecPerThread; ++j) {
     const int vi = j * kThreads + tid;  // strided groups: values 2048 apart
-    if (vi < si.nvc) {
-      bool partial;
-      uint32_t valid;
-      uint4 w = masked_vec(si, buf, vi, &partial, &valid);
-      if (partial) w = nan_fill(w, valid);
+    if (vi < nvc) {
+      uint4 w = lds128(buf + vi * 16);
+      if (vi == vlo || vi == vhi) w = nan_fill(w, valid_mask8(si.cv0 + vi, si.a0, si.a1));
       acc0 = h2_as_u32(__hmax2(u32_as_h2(acc0), u32_as_h2(w.x)));
       acc1 = h2_as_u32(__hmax2(u32_as_h2(acc1), u32_as_h2(w.y)));
       acc2 = h2_as_u32(__hmax2(u32_as_h2(acc2), u32_as_h2(w.z)));
@@ -517,7 +564,9 @@ __device__ uint32_t chunk_select(const TopkParams& p, const StageInfo& si, const
   csync();
   if (tid < 32) {  // lane l owns words [l * per, (l + 1) * per) of the nw * kThreads words
     const int per = nw * kThreads / 32;
-    const uint32_t K = kth_packed_keys(sm.gkeys + lane * per, per, static_cast<uint32_t>(p.k));
+    const uint32_t K = per == 8 ? kth_keys16(sm.gkeys + lane * 8, static_cast<uint32_t>(p.k))
+                                : kth_packed_keys(sm.gkeys + lane * per, per,
+                                                  static_cast<uint32_t>(p.k));
     if (lane == 0) sm.bcast[3] = K;
     if (lane == 0 && p.stats) atomicAdd(&p.status[3], 1u);
   }

@@ -237,10 +237,12 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
   int st = 0, par = 0;
   uint32_t ph = 0;   // full-barrier phase parity of stage st
   bool failed = false;
+  bool ready = false;  // stage st's full phase was already seen complete
   for (;;) {
     // A failed wait is noticed by everyone at the next barrier (sm.fail), so every consumer
     // thread keeps taking the same branches; stage info is never garbage (initialised).
-    if (!mbar_wait(&full[st], ph)) sm.fail = 1u;
+    if (!ready && !mbar_wait(&full[st], ph)) sm.fail = 1u;
+    ready = false;
     const StageInfo& si = info[st];  // read in place: valid until this stage is released
     if (si.part == kStopPart) break;
     if (si.nvc > 0) {
@@ -259,12 +261,17 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
       // certified a strict threshold, tie-heavy rows have nothing left to pass.
       bool done = false;
       if (ss.strict && ss.K < kNoThreshold && (ss.quiet || ss.mycnt == 1)) {
+        const bool last = si.last != 0;  // read before the barrier
         const uint32_t vb = key_to_bits(ss.K);
         uint32_t cnt;
         const uint32_t f = thread_flags<true>(si, buf, u32_as_h2(vb | (vb << 16)), false, &cnt);
+        // Query the next stage now: the query's latency overlaps the OR-barrier, and a stage
+        // that has landed needs no wait at the top of the loop (its phase cannot advance
+        // before this thread releases it).
+        ready = mbar_test_wait(&full[st + 1 == S ? 0 : st + 1], st + 1 == S ? ph ^ 1u : ph);
         done = !group_or<kThreads>(f != 0 || sm.fail != 0);
         if (done) ss.quiet = true;
-        if (done && si.last) {  // nothing passed in the part's last chunk: the end marker
+        if (done && last) {  // nothing passed in the part's last chunk: the end marker
           if (!wait_batch_free(sm, nb)) sm.fail = 1u;  // seen by all at the next barrier
           BatchMeta meta;
           meta.len = si.a1 - si.a0;
