@@ -150,6 +150,25 @@ cudaError_t device_info(DeviceInfo* out) {
 
 // The streaming kernel with programmatic stream serialisation: its prologue overlaps the
 // set-up kernel, which it waits for (grid_dep_wait) before touching the workspace.
+// The set-up kernels are launched with programmatic stream serialisation as well: behind the
+// previous call's streaming kernel (which lets dependents launch early) their blocks are placed
+// while it drains, and each waits (griddepcontrol.wait) for the preceding grid to complete
+// before touching the workspace.  Behind any other kernel this is plain stream order.
+cudaError_t launch_setup(void (*kernel)(TopkParams), const TopkParams& p, int grid, int threads,
+                         cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 template <bool BIG>
 cudaError_t launch_topk(const TopkParams& p, int grid, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
@@ -194,12 +213,10 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
     p.steal = (!big && per == 1 && p.tail_seg0 == p.seg_num && g_steal_env != 0) ? 1 : 0;
   }
   if (csr) {
-    csr_prep_kernel<<<1, 1024, 0, stream>>>(p);
+    e = launch_setup(csr_prep_kernel, p, 1, 1024, stream);
   } else {
-    const int blocks = static_cast<int>((p.seg_num + 255) / 256);
-    init_kernel<<<blocks, 256, 0, stream>>>(p);
+    e = launch_setup(init_kernel, p, static_cast<int>((p.seg_num + 255) / 256), 256, stream);
   }
-  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   long long grid_ll = parts < resident ? (parts > 0 ? parts : 1) : resident;
   if (g_grid_env > 0 && g_grid_env < grid_ll) grid_ll = g_grid_env;

@@ -1485,6 +1485,9 @@ topk_kernel(TopkParams p) {
   }
   __syncthreads();
   grid_dep_wait();  // the set-up kernel's resets are complete and visible from here on
+  // The next call's set-up kernel may launch now: it waits for this grid to complete (and
+  // its memory to be visible) before it touches the workspace, so only its launch overlaps.
+  grid_dep_launch();
   if (tid >= kThreads) {
     if (tid == kThreads) {
       producer_loop<BIG>(p, stages, full, empty, info);
@@ -1505,6 +1508,7 @@ topk_kernel(TopkParams p) {
 // Fixed-length rows: reset the per-segment thresholds, arrival counters and status words.
 __global__ void init_kernel(TopkParams p) {
   grid_dep_launch();  // the streaming kernel may set up meanwhile; it waits before any use
+  grid_dep_wait();    // launched early behind the previous kernel: wait for its completion
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   if (i < 16) p.status[i] = 0;
@@ -1522,6 +1526,7 @@ __global__ void init_kernel(TopkParams p) {
 __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
   __shared__ uint32_t warp_tot[32];
   grid_dep_launch();  // the streaming kernel may set up meanwhile; it waits before any use
+  grid_dep_wait();    // launched early behind the previous kernel: wait for its completion
   const int tid = threadIdx.x;
   if (tid < 16) p.status[tid] = 0;
   for (long long c = tid; c < p.slot_capacity; c += 1024) p.chunk_count[c] = 0;
