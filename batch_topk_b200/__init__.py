@@ -61,6 +61,32 @@ def batch_topk_half_segmented_workspace_size(seg_num: int, max_total_len: int, k
     return int(_lib.load().bt_topk_half_segmented_workspace_size(seg_num, max_total_len, k))
 
 
+def batch_topk_bf16(d_input: int, seg_num: int, seg_len: int, k: int, d_output_values: int,
+                    d_output_indices: int, d_workspace: int, workspace_bytes: int,
+                    stream: int = 0) -> int:
+    """batch_topk_half for bfloat16 rows (no reference counterpart): the same contract, with
+    values ordered as bfloat16."""
+    return _lib.load().bt_topk_bf16(d_input, seg_num, seg_len, k, d_output_values,
+                                    d_output_indices, d_workspace, workspace_bytes, stream)
+
+
+def batch_topk_bf16_workspace_size(seg_num: int, seg_len: int, k: int) -> int:
+    return int(_lib.load().bt_topk_bf16_workspace_size(seg_num, seg_len, k))
+
+
+def batch_topk_bf16_segmented(d_input: int, d_offsets: int, seg_num: int, max_total_len: int,
+                              k: int, d_output_values: int, d_output_indices: int,
+                              d_workspace: int, workspace_bytes: int, stream: int = 0) -> int:
+    """CSR variant for bfloat16 values (no reference counterpart); -inf (0xFF80) pads."""
+    return _lib.load().bt_topk_bf16_segmented(d_input, d_offsets, seg_num, max_total_len, k,
+                                              d_output_values, d_output_indices, d_workspace,
+                                              workspace_bytes, stream)
+
+
+def batch_topk_bf16_segmented_workspace_size(seg_num: int, max_total_len: int, k: int) -> int:
+    return int(_lib.load().bt_topk_bf16_segmented_workspace_size(seg_num, max_total_len, k))
+
+
 def batch_topk_half_noalloc(d_input: int, seg_num: int, seg_len: int, k: int,
                             d_output_values: int, d_output_indices: int, stream: int = 0) -> int:
     """bt_topk_half_noalloc (no reference counterpart): batch_topk_half on the library's fixed

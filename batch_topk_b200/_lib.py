@@ -17,6 +17,10 @@ EXPORTED = (
     "bt_topk_half_segmented",
     "bt_topk_half_segmented_workspace_size",
     "bt_topk_half_noalloc",
+    "bt_topk_bf16",
+    "bt_topk_bf16_workspace_size",
+    "bt_topk_bf16_segmented",
+    "bt_topk_bf16_segmented_workspace_size",
     "bt_workspace_status",
     "bt_set_profile_events",
     "bt_device_info",
@@ -53,6 +57,14 @@ def load() -> C.CDLL:
         lib.bt_topk_half_segmented_workspace_size.restype = sz
         lib.bt_topk_half_noalloc.argtypes = [vp, i32, i32, i32, vp, vp, vp]
         lib.bt_topk_half_noalloc.restype = i32
+        lib.bt_topk_bf16.argtypes = [vp, i32, i32, i32, vp, vp, vp, sz, vp]
+        lib.bt_topk_bf16.restype = i32
+        lib.bt_topk_bf16_workspace_size.argtypes = [i32, i32, i32]
+        lib.bt_topk_bf16_workspace_size.restype = sz
+        lib.bt_topk_bf16_segmented.argtypes = [vp, vp, i32, i64, i32, vp, vp, vp, sz, vp]
+        lib.bt_topk_bf16_segmented.restype = i32
+        lib.bt_topk_bf16_segmented_workspace_size.argtypes = [i32, i64, i32]
+        lib.bt_topk_bf16_segmented_workspace_size.restype = sz
         lib.bt_workspace_status.argtypes = [vp, i32, vp, C.POINTER(C.c_uint * 6)]
         lib.bt_workspace_status.restype = i32
         lib.bt_set_profile_events.argtypes = [vp, vp]

@@ -72,6 +72,14 @@ bool csr_shape_ok(int seg_num, long long max_total_len, int k) {
          max_total_len < (1ll << 31);
 }
 
+using TopkKernel = void (*)(TopkParams);
+
+// The streaming kernel for k <= 128 (small) or larger k, per element type.
+TopkKernel topk_kernel_for(bool big, bool bf16) {
+  if (bf16) return big ? bf16::topk_kernel<true> : bf16::topk_kernel<false>;
+  return big ? f16::topk_kernel<true> : f16::topk_kernel<false>;
+}
+
 struct DeviceInfo {
   bool ready = false;
   int sms = 0;
@@ -109,22 +117,26 @@ cudaError_t device_info(DeviceInfo* out) {
   std::lock_guard<std::mutex> lock(g_mu);
   DeviceInfo& d = g_dev[dev];
   if (!d.ready) {
-    e = cudaFuncSetAttribute(topk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(SmemLayout<false>::bytes));
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(SmemLayout<true>::bytes));
-    if (e != cudaSuccess) return e;
     e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.blocks_per_sm[0], topk_kernel<false>,
-                                                      block_threads<false>(),
-                                                      SmemLayout<false>::bytes);
-    if (e != cudaSuccess) return e;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.blocks_per_sm[1], topk_kernel<true>,
-                                                      block_threads<true>(),
-                                                      SmemLayout<true>::bytes);
-    if (e != cudaSuccess) return e;
+    // Both element types' kernels: the shared-memory opt-in, and the smaller occupancy of the
+    // two (the same code shape, so in practice the same number).
+    for (int big = 0; big < 2; ++big) {
+      const size_t smem = big ? SmemLayout<true>::bytes : SmemLayout<false>::bytes;
+      const int threads = big ? block_threads<true>() : block_threads<false>();
+      int best = 1 << 30;
+      for (int bf = 0; bf < 2; ++bf) {
+        const TopkKernel kern = topk_kernel_for(big != 0, bf != 0);
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        int n = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, smem);
+        if (e != cudaSuccess) return e;
+        best = n < best ? n : best;
+      }
+      d.blocks_per_sm[big] = best;
+    }
     if (d.blocks_per_sm[0] < 1 || d.blocks_per_sm[1] < 1) return cudaErrorInvalidConfiguration;
     if (g_stats < 0) {
       const char* s = std::getenv("BT_STATS");
@@ -170,7 +182,7 @@ cudaError_t launch_setup(void (*kernel)(TopkParams), const TopkParams& p, int gr
 }
 
 template <bool BIG>
-cudaError_t launch_topk(const TopkParams& p, int grid, cudaStream_t stream) {
+cudaError_t launch_topk(const TopkParams& p, int grid, bool bf16, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(static_cast<unsigned>(block_threads<BIG>()));
@@ -181,10 +193,11 @@ cudaError_t launch_topk(const TopkParams& p, int grid, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, topk_kernel<BIG>, p);
+  return cudaLaunchKernelEx(&cfg, topk_kernel_for(BIG, bf16), p);
 }
 
-cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaStream_t stream) {
+cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, bool bf16,
+                            cudaStream_t stream) {
   DeviceInfo di;
   cudaError_t e = device_info(&di);
   if (e != cudaSuccess) return e;
@@ -223,15 +236,17 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, cudaSt
   const int grid = static_cast<int>(grid_ll);
   p.help_window = p.steal ? (grid < p.seg_num ? grid : p.seg_num) : 0;
   if (g_prof_start) cudaEventRecord(g_prof_start, stream);
-  e = big ? launch_topk<true>(p, grid, stream) : launch_topk<false>(p, grid, stream);
+  e = big ? launch_topk<true>(p, grid, bf16, stream) : launch_topk<false>(p, grid, bf16, stream);
   if (e != cudaSuccess) return e;
   if (g_prof_stop) cudaEventRecord(g_prof_stop, stream);
   return cudaSuccess;
 }
 
 TopkParams base_params(const void* d_input, int seg_num, int k, void* d_out_values,
-                       int* d_out_indices, void* d_workspace, const Layout& L, long long slots) {
+                       int* d_out_indices, void* d_workspace, const Layout& L, long long slots,
+                       bool bf16) {
   TopkParams p{};
+  p.pad_bits = bf16 ? 0xFF80u : 0xFC00u;  // -inf
   const uintptr_t in = reinterpret_cast<uintptr_t>(d_input);
   p.base = reinterpret_cast<const uint16_t*>(in & ~static_cast<uintptr_t>(15));
   p.shift = static_cast<int>((in & 15) / 2);
@@ -260,6 +275,46 @@ bool pointers_ok(const void* in, const void* ov, const int* oi, const void* ws) 
   const uintptr_t a = reinterpret_cast<uintptr_t>(in), b = reinterpret_cast<uintptr_t>(ov),
                   c = reinterpret_cast<uintptr_t>(oi), d = reinterpret_cast<uintptr_t>(ws);
   return (a % 2 == 0) && (b % 2 == 0) && (c % 4 == 0) && (d % 16 == 0);
+}
+
+// Fixed-length rows of 16-bit values (fp16, or bf16 when bf16 is set).
+int topk_fixed(const void* d_input, int seg_num, int seg_len, int k, void* d_output_values,
+               int* d_output_indices, void* d_workspace, size_t workspace_bytes, void* stream,
+               bool bf16) {
+  if (!fixed_shape_ok(seg_num, seg_len, k)) return cudaErrorInvalidValue;
+  if (!pointers_ok(d_input, d_output_values, d_output_indices, d_workspace)) {
+    return cudaErrorInvalidValue;
+  }
+  const long long p_max = slots_per_segment(seg_len);
+  const long long slots = static_cast<long long>(seg_num) * p_max;
+  const Layout L = make_layout(seg_num, slots, cap_for_k(k), false);
+  if (workspace_bytes < L.total) return cudaErrorInvalidValue;
+  TopkParams p = base_params(d_input, seg_num, k, d_output_values, d_output_indices,
+                             d_workspace, L, slots, bf16);
+  p.seg_len = seg_len;
+  p.offsets = nullptr;
+  p.p_max = static_cast<int>(p_max);
+  return launch_pipeline(p, false, slots, bf16, static_cast<cudaStream_t>(stream));
+}
+
+// CSR batches of 16-bit values (fp16, or bf16 when bf16 is set).
+int topk_csr(const void* d_input, const int* d_offsets, int seg_num, long long max_total_len,
+             int k, void* d_output_values, int* d_output_indices, void* d_workspace,
+             size_t workspace_bytes, void* stream, bool bf16) {
+  if (!csr_shape_ok(seg_num, max_total_len, k)) return cudaErrorInvalidValue;
+  if (!d_offsets || reinterpret_cast<uintptr_t>(d_offsets) % 4 != 0) return cudaErrorInvalidValue;
+  if (!pointers_ok(d_input, d_output_values, d_output_indices, d_workspace)) {
+    return cudaErrorInvalidValue;
+  }
+  const long long slots = csr_slot_bound(seg_num, max_total_len);
+  const Layout L = make_layout(seg_num, slots, cap_for_k(k), true);
+  if (workspace_bytes < L.total) return cudaErrorInvalidValue;
+  TopkParams p = base_params(d_input, seg_num, k, d_output_values, d_output_indices,
+                             d_workspace, L, slots, bf16);
+  p.seg_len = 0;
+  p.offsets = d_offsets;
+  p.p_max = 0;
+  return launch_pipeline(p, true, slots, bf16, static_cast<cudaStream_t>(stream));
 }
 
 }  // namespace
@@ -308,20 +363,8 @@ size_t bt_topk_half_workspace_size(int seg_num, int seg_len, int k) {
 
 int bt_topk_half(const void* d_input, int seg_num, int seg_len, int k, void* d_output_values,
                  int* d_output_indices, void* d_workspace, size_t workspace_bytes, void* stream) {
-  if (!bt::fixed_shape_ok(seg_num, seg_len, k)) return cudaErrorInvalidValue;
-  if (!bt::pointers_ok(d_input, d_output_values, d_output_indices, d_workspace)) {
-    return cudaErrorInvalidValue;
-  }
-  const long long p_max = bt::slots_per_segment(seg_len);
-  const long long slots = static_cast<long long>(seg_num) * p_max;
-  const bt::Layout L = bt::make_layout(seg_num, slots, bt::cap_for_k(k), false);
-  if (workspace_bytes < L.total) return cudaErrorInvalidValue;
-  bt::TopkParams p = bt::base_params(d_input, seg_num, k, d_output_values, d_output_indices,
-                                     d_workspace, L, slots);
-  p.seg_len = seg_len;
-  p.offsets = nullptr;
-  p.p_max = static_cast<int>(p_max);
-  return bt::launch_pipeline(p, false, slots, static_cast<cudaStream_t>(stream));
+  return bt::topk_fixed(d_input, seg_num, seg_len, k, d_output_values, d_output_indices,
+                        d_workspace, workspace_bytes, stream, false);
 }
 
 int bt_topk_half_noalloc(const void* d_input, int seg_num, int seg_len, int k,
@@ -351,20 +394,30 @@ int bt_topk_half_segmented(const void* d_input, const int* d_offsets, int seg_nu
                            long long max_total_len, int k, void* d_output_values,
                            int* d_output_indices, void* d_workspace, size_t workspace_bytes,
                            void* stream) {
-  if (!bt::csr_shape_ok(seg_num, max_total_len, k)) return cudaErrorInvalidValue;
-  if (!d_offsets || reinterpret_cast<uintptr_t>(d_offsets) % 4 != 0) return cudaErrorInvalidValue;
-  if (!bt::pointers_ok(d_input, d_output_values, d_output_indices, d_workspace)) {
-    return cudaErrorInvalidValue;
-  }
-  const long long slots = bt::csr_slot_bound(seg_num, max_total_len);
-  const bt::Layout L = bt::make_layout(seg_num, slots, bt::cap_for_k(k), true);
-  if (workspace_bytes < L.total) return cudaErrorInvalidValue;
-  bt::TopkParams p = bt::base_params(d_input, seg_num, k, d_output_values, d_output_indices,
-                                     d_workspace, L, slots);
-  p.seg_len = 0;
-  p.offsets = d_offsets;
-  p.p_max = 0;
-  return bt::launch_pipeline(p, true, slots, static_cast<cudaStream_t>(stream));
+  return bt::topk_csr(d_input, d_offsets, seg_num, max_total_len, k, d_output_values,
+                      d_output_indices, d_workspace, workspace_bytes, stream, false);
+}
+
+size_t bt_topk_bf16_workspace_size(int seg_num, int seg_len, int k) {
+  return bt_topk_half_workspace_size(seg_num, seg_len, k);
+}
+
+int bt_topk_bf16(const void* d_input, int seg_num, int seg_len, int k, void* d_output_values,
+                 int* d_output_indices, void* d_workspace, size_t workspace_bytes, void* stream) {
+  return bt::topk_fixed(d_input, seg_num, seg_len, k, d_output_values, d_output_indices,
+                        d_workspace, workspace_bytes, stream, true);
+}
+
+size_t bt_topk_bf16_segmented_workspace_size(int seg_num, long long max_total_len, int k) {
+  return bt_topk_half_segmented_workspace_size(seg_num, max_total_len, k);
+}
+
+int bt_topk_bf16_segmented(const void* d_input, const int* d_offsets, int seg_num,
+                           long long max_total_len, int k, void* d_output_values,
+                           int* d_output_indices, void* d_workspace, size_t workspace_bytes,
+                           void* stream) {
+  return bt::topk_csr(d_input, d_offsets, seg_num, max_total_len, k, d_output_values,
+                      d_output_indices, d_workspace, workspace_bytes, stream, true);
 }
 
 int bt_workspace_status(const void* d_workspace, int seg_num, void* stream, unsigned* stats) {

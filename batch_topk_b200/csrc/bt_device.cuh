@@ -1,12 +1,13 @@
-// bt_device.cuh -- shared device primitives for the batched fp16 top-k kernels (sm_100a).
+// bt_device.cuh -- shared device primitives for the batched top-k kernels (sm_100a).
 //
-//   * the fp16 descending key codec (reference: include/type_codec.cuh:13-38);
+//   * the inverse of the descending key codec (the codec itself: bt_elem.cuh);
 //   * mbarrier and bulk-copy (cp.async.bulk, no multicast) wrappers with bounded waits;
 //   * block scans, bin search over 256-bin histograms, and aggregated smem histogram adds.
 #pragma once
 
 #include <cstdint>
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 namespace bt {
@@ -33,63 +34,12 @@ constexpr uint32_t kStatusBadOffsets = 2;
 constexpr uint32_t kStatusSegmentTooLong = 4;
 constexpr uint32_t kStatusCertifyFailed = 8;
 
-// ---- codec -------------------------------------------------------------------------
-// Descending key: smaller key ranks first.  Any NaN -> 0xFFFF (last); +-0 -> 0x7FFF;
-// otherwise key = bits ^ (sign ? 0x0000 : 0x7FFF), which is ~encode_half_asc.
-__host__ __device__ __forceinline__ uint32_t desc_key(uint32_t bits) {
-  bits &= 0xFFFFu;
-  if ((bits & 0x7C00u) == 0x7C00u && (bits & 0x03FFu) != 0) return 0xFFFFu;
-  if ((bits & 0x7FFFu) == 0) return 0x7FFFu;
-  return (bits & 0x8000u) ? bits : (bits ^ 0x7FFFu);
-}
-
-// fp16 bit pattern of the (non-NaN) value whose key is `key` (+0 for key 0x7FFF).
+// ---- codec (element-independent part) ---------------------------------------------
+// The descending key codec itself (NaN test, +-0) depends on the element type: bt_elem.cuh.
+// Bit pattern of the (non-NaN) value whose key is `key` (+0 for key 0x7FFF): the inverse map
+// is the same for fp16 and bf16.
 __host__ __device__ __forceinline__ uint32_t key_to_bits(uint32_t key) {
   return key < 0x8000u ? (key ^ 0x7FFFu) : key;
-}
-
-__device__ __forceinline__ __half2 u32_as_h2(uint32_t w) {
-  __half2 h;
-  *reinterpret_cast<uint32_t*>(&h) = w;
-  return h;
-}
-
-__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-
-// Bit e (e = 0..7, element order) set when element e of the vector is >= v (NaN: never).
-__device__ __forceinline__ uint32_t ge_mask8(const uint4& w, __half2 v2) {
-  const uint32_t m0 = __hge2_mask(u32_as_h2(w.x), v2);
-  const uint32_t m1 = __hge2_mask(u32_as_h2(w.y), v2);
-  const uint32_t m2 = __hge2_mask(u32_as_h2(w.z), v2);
-  const uint32_t m3 = __hge2_mask(u32_as_h2(w.w), v2);
-  const uint32_t x = (m0 & 0x00020001u) | (m1 & 0x00080004u) | (m2 & 0x00200010u) |
-                     (m3 & 0x00800040u);
-  return (x | (x >> 16)) & 0xFFu;
-}
-
-// Bit e set when element e is > v (NaN: never).
-__device__ __forceinline__ uint32_t gt_mask8(const uint4& w, __half2 v2) {
-  const uint32_t m0 = __hgt2_mask(u32_as_h2(w.x), v2);
-  const uint32_t m1 = __hgt2_mask(u32_as_h2(w.y), v2);
-  const uint32_t m2 = __hgt2_mask(u32_as_h2(w.z), v2);
-  const uint32_t m3 = __hgt2_mask(u32_as_h2(w.w), v2);
-  const uint32_t x = (m0 & 0x00020001u) | (m1 & 0x00080004u) | (m2 & 0x00200010u) |
-                     (m3 & 0x00800040u);
-  return (x | (x >> 16)) & 0xFFu;
-}
-
-// Replace the halves whose bit is clear in valid8 by a NaN (ignored by __hmax2).
-__device__ __forceinline__ uint32_t nan_fill_word(uint32_t w, uint32_t valid2) {
-  const uint32_t keep = ((valid2 & 1u) ? 0x0000FFFFu : 0u) | ((valid2 & 2u) ? 0xFFFF0000u : 0u);
-  return (w & keep) | (0x7E007E00u & ~keep);
-}
-
-__device__ __forceinline__ uint4 nan_fill(uint4 w, uint32_t valid8) {
-  w.x = nan_fill_word(w.x, valid8);
-  w.y = nan_fill_word(w.y, valid8 >> 2);
-  w.z = nan_fill_word(w.z, valid8 >> 4);
-  w.w = nan_fill_word(w.w, valid8 >> 6);
-  return w;
 }
 
 // 8-bit mask of the elements of aligned vector gv that lie inside [a0, a1).

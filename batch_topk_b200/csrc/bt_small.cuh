@@ -8,10 +8,9 @@
 // at lower indices, already exist).  At the segment's last chunk the list is the answer.
 // A segment shared by two blocks goes through global partial lists and an arrival counter;
 // the last block to arrive merges them.
-#pragma once
+// No include guard: part of bt_body.cuh, compiled once per element namespace.
 
 
-namespace bt {
 
 // ---- consumer ----------------------------------------------------------------------------
 
@@ -31,7 +30,7 @@ __device__ __forceinline__ Counted count_chunk(const StageInfo& si, const uint8_
   const int warp = tid >> 5;
   const bool take_all = K == kNoThreshold;
   const uint32_t vb = key_to_bits(K);
-  const __half2 v2 = u32_as_h2(vb | (vb << 16));
+  const h2t v2 = u32_as_h2(vb | (vb << 16));
   Counted c;
   c.flags = thread_flags<STRICT>(si, buf, v2, take_all, &c.cnt);
   uint32_t incl = 0;
@@ -74,7 +73,7 @@ __device__ __forceinline__ void write_batch(const StageInfo& si, const uint8_t* 
   const int tid = threadIdx.x;
   const bool take_all = K == kNoThreshold;
   const uint32_t vb = key_to_bits(K);
-  const __half2 v2 = u32_as_h2(vb | (vb << 16));
+  const h2t v2 = u32_as_h2(vb | (vb << 16));
   const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf);
   const long long e0 = si.cv0 * 8;
   uint32_t r = 0;
@@ -454,7 +453,7 @@ __device__ __forceinline__ void emit_row(const TopkParams& p, int s, const unsig
         ov[pos] = static_cast<uint16_t>(L[r] & 0xFFFFu);
         oi[pos] = static_cast<int>((L[r] >> 16) & 0xFFFFFFFFu);
       } else {
-        ov[pos] = 0xFC00u;
+        ov[pos] = kNegInfBits;
         oi[pos] = -1;
       }
     }
@@ -580,4 +579,3 @@ __device__ void merger_loop(const TopkParams& p, SmallScratch& sm) {
   }
 }
 
-}  // namespace bt

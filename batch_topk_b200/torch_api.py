@@ -1,9 +1,9 @@
 """Tensor-level helpers over the C ABI (PyTorch provides device memory and streams only).
 
-    values, indices = topk(x, k)                      # x: [seg_num, seg_len] fp16 on CUDA
-    values, indices = topk_segmented(x, offsets, k)   # x: 1-D fp16, offsets: int32 [seg_num+1]
+    values, indices = topk(x, k)                      # x: [seg_num, seg_len] fp16/bf16 on CUDA
+    values, indices = topk_segmented(x, offsets, k)   # x: 1-D fp16/bf16, offsets: int32 [seg_num+1]
 
-Values come back as fp16 (the input's own bit patterns), indices as int32, both
+Values come back in x's dtype (the input's own bit patterns), indices as int32, both
 [seg_num, k]; descending by value, lower index first among equal values, NaN last.
 """
 from __future__ import annotations
@@ -12,11 +12,23 @@ import torch
 
 from . import (
     BatchTopkError,
+    batch_topk_bf16,
+    batch_topk_bf16_segmented,
+    batch_topk_bf16_segmented_workspace_size,
+    batch_topk_bf16_workspace_size,
     batch_topk_half,
     batch_topk_half_segmented,
     batch_topk_half_segmented_workspace_size,
     batch_topk_half_workspace_size,
 )
+
+# entry points per element type: (fixed, fixed workspace size, CSR, CSR workspace size)
+_ENTRY = {
+    torch.float16: (batch_topk_half, batch_topk_half_workspace_size, batch_topk_half_segmented,
+                    batch_topk_half_segmented_workspace_size),
+    torch.bfloat16: (batch_topk_bf16, batch_topk_bf16_workspace_size, batch_topk_bf16_segmented,
+                     batch_topk_bf16_segmented_workspace_size),
+}
 
 
 class Workspace:
@@ -51,49 +63,50 @@ def _stream(device, stream):
 
 def topk(x: torch.Tensor, k: int, *, workspace: Workspace | None = None, stream=None,
          out: tuple | None = None):
-    if x.dtype != torch.float16 or x.dim() != 2 or not x.is_cuda:
-        raise ValueError("x must be a 2-D float16 CUDA tensor")
+    if x.dtype not in _ENTRY or x.dim() != 2 or not x.is_cuda:
+        raise ValueError("x must be a 2-D float16 or bfloat16 CUDA tensor")
+    run, size, _, _ = _ENTRY[x.dtype]
     x = x.contiguous()
     seg_num, seg_len = x.shape
-    nbytes = batch_topk_half_workspace_size(seg_num, seg_len, k)
+    nbytes = size(seg_num, seg_len, k)
     if nbytes == 0:
         raise BatchTopkError(1, f"unsupported shape ({seg_num}, {seg_len}, k={k})")
     ws = _ws(x.device, workspace).get(nbytes)
     if out is None:
-        vals = torch.empty((seg_num, k), dtype=torch.float16, device=x.device)
+        vals = torch.empty((seg_num, k), dtype=x.dtype, device=x.device)
         idx = torch.empty((seg_num, k), dtype=torch.int32, device=x.device)
     else:
         vals, idx = out
-    rc = batch_topk_half(x.data_ptr(), seg_num, seg_len, k, vals.data_ptr(), idx.data_ptr(),
-                         ws.data_ptr(), ws.numel(), _stream(x.device, stream))
+    rc = run(x.data_ptr(), seg_num, seg_len, k, vals.data_ptr(), idx.data_ptr(), ws.data_ptr(),
+             ws.numel(), _stream(x.device, stream))
     if rc != 0:
-        raise BatchTopkError(rc, "bt_topk_half")
+        raise BatchTopkError(rc, "top-k")
     return vals, idx
 
 
 def topk_segmented(x: torch.Tensor, offsets: torch.Tensor, k: int, *,
                    max_total_len: int | None = None, workspace: Workspace | None = None,
                    stream=None, out: tuple | None = None):
-    if x.dtype != torch.float16 or x.dim() != 1 or not x.is_cuda:
-        raise ValueError("x must be a 1-D float16 CUDA tensor")
+    if x.dtype not in _ENTRY or x.dim() != 1 or not x.is_cuda:
+        raise ValueError("x must be a 1-D float16 or bfloat16 CUDA tensor")
+    _, _, run, size = _ENTRY[x.dtype]
     if offsets.dtype != torch.int32 or offsets.dim() != 1 or offsets.device != x.device:
         raise ValueError("offsets must be a 1-D int32 tensor on x's device")
     seg_num = offsets.numel() - 1
     total = x.numel() if max_total_len is None else max_total_len
-    nbytes = batch_topk_half_segmented_workspace_size(seg_num, total, k)
+    nbytes = size(seg_num, total, k)
     if nbytes == 0:
         raise BatchTopkError(1, f"unsupported CSR batch (seg_num={seg_num}, k={k})")
     ws = _ws(x.device, workspace).get(nbytes)
     if out is None:
-        vals = torch.empty((seg_num, k), dtype=torch.float16, device=x.device)
+        vals = torch.empty((seg_num, k), dtype=x.dtype, device=x.device)
         idx = torch.empty((seg_num, k), dtype=torch.int32, device=x.device)
     else:
         vals, idx = out
-    rc = batch_topk_half_segmented(x.data_ptr(), offsets.data_ptr(), seg_num, total, k,
-                                   vals.data_ptr(), idx.data_ptr(), ws.data_ptr(), ws.numel(),
-                                   _stream(x.device, stream))
+    rc = run(x.data_ptr(), offsets.data_ptr(), seg_num, total, k, vals.data_ptr(),
+             idx.data_ptr(), ws.data_ptr(), ws.numel(), _stream(x.device, stream))
     if rc != 0:
-        raise BatchTopkError(rc, "bt_topk_half_segmented")
+        raise BatchTopkError(rc, "segmented top-k")
     return vals, idx
 
 
@@ -145,8 +158,8 @@ def _topk_op(x: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
 
 @_topk_op.register_fake
 def _topk_op_fake(x: torch.Tensor, k: int):
-    if x.dim() != 2 or x.dtype != torch.float16:
-        raise ValueError("x must be a 2-D float16 tensor")
+    if x.dim() != 2 or x.dtype not in _ENTRY:
+        raise ValueError("x must be a 2-D float16 or bfloat16 tensor")
     return (x.new_empty((x.shape[0], k)), x.new_empty((x.shape[0], k), dtype=torch.int32))
 
 

@@ -58,6 +58,24 @@ int bt_topk_half_segmented(const void* d_input, const int* d_offsets, int seg_nu
 
 size_t bt_topk_half_segmented_workspace_size(int seg_num, long long max_total_len, int k);
 
+/* bfloat16 inputs; no reference counterpart (the reference is fp16 only and lists other types
+ * as a non-goal).  The same arguments, layouts, limits, error contract and order as the fp16
+ * entry points above, with values ordered as bfloat16: descending, equal values by lower
+ * index, -0 equal to +0, NaN last.  Output values are the input's own bit patterns; a missing
+ * entry of a short CSR segment is -inf (0xFF80) with index -1.  The workspace sizes are those
+ * of the fp16 entry points. */
+int bt_topk_bf16(const void* d_input, int seg_num, int seg_len, int k, void* d_output_values,
+                 int* d_output_indices, void* d_workspace, size_t workspace_bytes, void* stream);
+
+size_t bt_topk_bf16_workspace_size(int seg_num, int seg_len, int k);
+
+int bt_topk_bf16_segmented(const void* d_input, const int* d_offsets, int seg_num,
+                           long long max_total_len, int k, void* d_output_values,
+                           int* d_output_indices, void* d_workspace, size_t workspace_bytes,
+                           void* stream);
+
+size_t bt_topk_bf16_segmented_workspace_size(int seg_num, long long max_total_len, int k);
+
 /* bt_topk_half without a caller workspace; NO COUNTERPART IN THE REFERENCE, which always takes
  * a caller-allocated workspace (include/batch_topk.cuh:10-19).
  *

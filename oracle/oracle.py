@@ -52,6 +52,14 @@ class Oracle:
         lib.oracle_topk_batch.restype = C.c_int
         lib.oracle_topk_csr.argtypes = [u16p, i64p, C.c_int64, C.c_int, u16p, i32p, C.c_int, C.c_int]
         lib.oracle_topk_csr.restype = C.c_int
+        lib.oracle_topk_batch_bf16.argtypes = lib.oracle_topk_batch.argtypes
+        lib.oracle_topk_batch_bf16.restype = C.c_int
+        lib.oracle_topk_csr_bf16.argtypes = lib.oracle_topk_csr.argtypes
+        lib.oracle_topk_csr_bf16.restype = C.c_int
+        lib.oracle_encode_desc_bf16.argtypes = [C.c_uint16]
+        lib.oracle_encode_desc_bf16.restype = C.c_uint16
+        lib.oracle_bf16_to_float.argtypes = [C.c_uint16]
+        lib.oracle_bf16_to_float.restype = C.c_float
         lib.oracle_encode_desc.argtypes = [C.c_uint16]
         lib.oracle_encode_desc.restype = C.c_uint16
         lib.oracle_half_to_float.argtypes = [C.c_uint16]
@@ -63,28 +71,30 @@ class Oracle:
         self.lib = lib
 
     def topk(self, values_bits: np.ndarray, k: int, method: int = METHOD_COUNT,
-             threads: int | None = None):
-        """Top-k of each row of a 2-D uint16 (fp16 bit pattern) array."""
+             threads: int | None = None, bf16: bool = False):
+        """Top-k of each row of a 2-D uint16 array of fp16 (or, with bf16, bfloat16) bits."""
         x = np.ascontiguousarray(values_bits, dtype=np.uint16)
         assert x.ndim == 2
         seg_num, seg_len = x.shape
         ov = np.empty((seg_num, k), np.uint16)
         oi = np.empty((seg_num, k), np.int32)
-        rc = self.lib.oracle_topk_batch(x.reshape(-1), seg_num, seg_len, k, ov.reshape(-1),
-                                        oi.reshape(-1), method, threads or os.cpu_count() or 1)
+        fn = self.lib.oracle_topk_batch_bf16 if bf16 else self.lib.oracle_topk_batch
+        rc = fn(x.reshape(-1), seg_num, seg_len, k, ov.reshape(-1), oi.reshape(-1), method,
+                threads or os.cpu_count() or 1)
         if rc != 0:
             raise ValueError("oracle_topk_batch rejected the arguments")
         return ov, oi
 
     def topk_csr(self, values_bits: np.ndarray, offsets: np.ndarray, k: int,
-                 method: int = METHOD_COUNT, threads: int | None = None):
+                 method: int = METHOD_COUNT, threads: int | None = None, bf16: bool = False):
         x = np.ascontiguousarray(values_bits, dtype=np.uint16).reshape(-1)
         off = np.ascontiguousarray(offsets, dtype=np.int64)
         seg_num = off.shape[0] - 1
         ov = np.empty((seg_num, k), np.uint16)
         oi = np.empty((seg_num, k), np.int32)
-        rc = self.lib.oracle_topk_csr(x, off, seg_num, k, ov.reshape(-1), oi.reshape(-1), method,
-                                      threads or os.cpu_count() or 1)
+        fn = self.lib.oracle_topk_csr_bf16 if bf16 else self.lib.oracle_topk_csr
+        rc = fn(x, off, seg_num, k, ov.reshape(-1), oi.reshape(-1), method,
+                threads or os.cpu_count() or 1)
         if rc != 0:
             raise ValueError("oracle_topk_csr rejected the arguments")
         return ov, oi
@@ -178,7 +188,9 @@ def load() -> Oracle:
     global _oracle
     with _lock:
         if _oracle is None:
-            if not os.path.exists(LIB_PATH):
+            src = os.path.join(HERE, "topk_oracle.c")
+            if not os.path.exists(LIB_PATH) or (
+                    os.path.exists(src) and os.path.getmtime(src) > os.path.getmtime(LIB_PATH)):
                 build(ref=False)
             _oracle = Oracle()
         return _oracle

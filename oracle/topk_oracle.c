@@ -26,6 +26,11 @@
  *
  * Short segments (len < k) produce len entries; the batch drivers pad the rest of the row
  * with value 0xFC00 (-inf) and index -1.
+ *
+ * bfloat16 rows (the *_bf16 drivers): the reference has no bf16 path (other input types are
+ * a listed non-goal), so this restates the same comparator on bfloat16 values converted
+ * exactly to float, and the same descending key with bfloat16's NaN test (exponent field
+ * 0x7F80); padding is bfloat16 -inf, 0xFF80.
  */
 #include <math.h>
 #include <pthread.h>
@@ -47,6 +52,23 @@ uint16_t oracle_encode_asc(uint16_t raw) {
 }
 
 uint16_t oracle_encode_desc(uint16_t raw) { return (uint16_t)~oracle_encode_asc(raw); }
+
+/* bfloat16: the same sign-magnitude codec with an 8-bit exponent field. */
+uint16_t oracle_encode_desc_bf16(uint16_t raw) {
+  uint16_t bits = raw;
+  if ((bits & 0x7fffu) > 0x7f80u) bits = 0xffffu; /* any NaN */
+  else if ((bits & 0x7fffu) == 0) bits = 0x0000u; /* +-0 */
+  const uint16_t asc = (bits & 0x8000u) ? (uint16_t)~bits : (uint16_t)(bits ^ 0x8000u);
+  return (uint16_t)~asc;
+}
+
+/* Exact bfloat16 -> fp32 conversion (bfloat16 is the top half of an fp32). */
+float oracle_bf16_to_float(uint16_t b) {
+  const uint32_t f = (uint32_t)b << 16;
+  float out;
+  memcpy(&out, &f, sizeof(out));
+  return out;
+}
 
 /* Exact fp16 -> fp32 conversion (every fp16 value is representable in fp32). */
 float oracle_half_to_float(uint16_t h) {
@@ -103,13 +125,14 @@ static void merge_sort_idx(const float* v, int* idx, int* tmp, int n) {
 }
 
 /* method 0: the reference's algorithm (sort whole permutation, take min(k,len)). */
-static int topk_sort_segment(const uint16_t* in, int len, int k, uint16_t* out_v, int32_t* out_i) {
+static int topk_sort_segment(const uint16_t* in, int len, int k, uint16_t* out_v, int32_t* out_i,
+                             int bf16) {
   if (len <= 0 || k <= 0) return 0;
   float* v = (float*)malloc(sizeof(float) * (size_t)len);
   int* idx = (int*)malloc(sizeof(int) * (size_t)len);
   int* tmp = (int*)malloc(sizeof(int) * (size_t)len);
   for (int i = 0; i < len; ++i) {
-    v[i] = oracle_half_to_float(in[i]);
+    v[i] = bf16 ? oracle_bf16_to_float(in[i]) : oracle_half_to_float(in[i]);
     idx[i] = i;
   }
   merge_sort_idx(v, idx, tmp, len);
@@ -130,13 +153,15 @@ static int cmp_key_idx(const void* a, const void* b) {
   return x < y ? -1 : (x > y ? 1 : 0);
 }
 
-static int topk_count_segment(const uint16_t* in, int len, int k, uint16_t* out_v, int32_t* out_i) {
+static int topk_count_segment(const uint16_t* in, int len, int k, uint16_t* out_v, int32_t* out_i,
+                              int bf16) {
   if (len <= 0 || k <= 0) return 0;
+  uint16_t (*encode)(uint16_t) = bf16 ? oracle_encode_desc_bf16 : oracle_encode_desc;
   const int kk = k < len ? k : len;
   uint32_t h1[256], h2[256];
   memset(h1, 0, sizeof(h1));
   memset(h2, 0, sizeof(h2));
-  for (int i = 0; i < len; ++i) ++h1[oracle_encode_desc(in[i]) >> 8];
+  for (int i = 0; i < len; ++i) ++h1[encode(in[i]) >> 8];
   uint32_t cum = 0;
   int b1 = 0;
   for (; b1 < 256; ++b1) {
@@ -144,7 +169,7 @@ static int topk_count_segment(const uint16_t* in, int len, int k, uint16_t* out_
     cum += h1[b1];
   }
   for (int i = 0; i < len; ++i) {
-    const uint16_t key = oracle_encode_desc(in[i]);
+    const uint16_t key = encode(in[i]);
     if ((key >> 8) == b1) ++h2[key & 0xffu];
   }
   int b2 = 0;
@@ -157,7 +182,7 @@ static int topk_count_segment(const uint16_t* in, int len, int k, uint16_t* out_
   uint64_t* sel = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)kk);
   int n = 0;
   for (int i = 0; i < len; ++i) {
-    const uint16_t key = oracle_encode_desc(in[i]);
+    const uint16_t key = encode(in[i]);
     if (key < cutoff || (key == cutoff && need > 0)) {
       if (key == cutoff) --need;
       sel[n++] = ((uint64_t)key << 32) | (uint32_t)i;
@@ -173,10 +198,15 @@ static int topk_count_segment(const uint16_t* in, int len, int k, uint16_t* out_
   return n;
 }
 
+static int topk_segment(const uint16_t* in, int len, int k, uint16_t* out_v, int32_t* out_i,
+                        int method, int bf16) {
+  return method == 0 ? topk_sort_segment(in, len, k, out_v, out_i, bf16)
+                     : topk_count_segment(in, len, k, out_v, out_i, bf16);
+}
+
 int oracle_topk_segment(const uint16_t* in, int len, int k, uint16_t* out_v, int32_t* out_i,
                         int method) {
-  return method == 0 ? topk_sort_segment(in, len, k, out_v, out_i)
-                     : topk_count_segment(in, len, k, out_v, out_i);
+  return topk_segment(in, len, k, out_v, out_i, method, 0);
 }
 
 /* ---- batch drivers (fixed-length rows and CSR offsets), threaded ------------------ */
@@ -187,6 +217,7 @@ typedef struct {
   int64_t seg_len;
   int k;
   int method;
+  int bf16;
   uint16_t* out_v;
   int32_t* out_i;
   int64_t seg_begin, seg_end;
@@ -205,9 +236,9 @@ static void* run_job(void* arg) {
     }
     uint16_t* ov = j->out_v + s * (int64_t)j->k;
     int32_t* oi = j->out_i + s * (int64_t)j->k;
-    int n = oracle_topk_segment(j->in + start, (int)len, j->k, ov, oi, j->method);
+    int n = topk_segment(j->in + start, (int)len, j->k, ov, oi, j->method, j->bf16);
     for (int r = n; r < j->k; ++r) {
-      ov[r] = 0xfc00u;
+      ov[r] = j->bf16 ? 0xff80u : 0xfc00u;
       oi[r] = -1;
     }
   }
@@ -215,7 +246,7 @@ static void* run_job(void* arg) {
 }
 
 static int run_batch(const uint16_t* in, const int64_t* offsets, int64_t seg_num, int64_t seg_len,
-                     int k, uint16_t* out_v, int32_t* out_i, int method, int threads) {
+                     int k, uint16_t* out_v, int32_t* out_i, int method, int threads, int bf16) {
   if (seg_num <= 0 || k <= 0) return -1;
   if (threads < 1) threads = 1;
   if (threads > seg_num) threads = (int)seg_num;
@@ -227,6 +258,7 @@ static int run_batch(const uint16_t* in, const int64_t* offsets, int64_t seg_num
     jobs[t].seg_len = seg_len;
     jobs[t].k = k;
     jobs[t].method = method;
+    jobs[t].bf16 = bf16;
     jobs[t].out_v = out_v;
     jobs[t].out_i = out_i;
     jobs[t].seg_begin = seg_num * t / threads;
@@ -242,12 +274,23 @@ static int run_batch(const uint16_t* in, const int64_t* offsets, int64_t seg_num
 int oracle_topk_batch(const uint16_t* in, int64_t seg_num, int64_t seg_len, int k, uint16_t* out_v,
                       int32_t* out_i, int method, int threads) {
   if (seg_len <= 0) return -1;
-  return run_batch(in, NULL, seg_num, seg_len, k, out_v, out_i, method, threads);
+  return run_batch(in, NULL, seg_num, seg_len, k, out_v, out_i, method, threads, 0);
 }
 
 int oracle_topk_csr(const uint16_t* in, const int64_t* offsets, int64_t seg_num, int k,
                     uint16_t* out_v, int32_t* out_i, int method, int threads) {
-  return run_batch(in, offsets, seg_num, 0, k, out_v, out_i, method, threads);
+  return run_batch(in, offsets, seg_num, 0, k, out_v, out_i, method, threads, 0);
+}
+
+int oracle_topk_batch_bf16(const uint16_t* in, int64_t seg_num, int64_t seg_len, int k,
+                           uint16_t* out_v, int32_t* out_i, int method, int threads) {
+  if (seg_len <= 0) return -1;
+  return run_batch(in, NULL, seg_num, seg_len, k, out_v, out_i, method, threads, 1);
+}
+
+int oracle_topk_csr_bf16(const uint16_t* in, const int64_t* offsets, int64_t seg_num, int k,
+                         uint16_t* out_v, int32_t* out_i, int method, int threads) {
+  return run_batch(in, offsets, seg_num, 0, k, out_v, out_i, method, threads, 1);
 }
 
 /* ---- select-state restatements, for the reference's known-answer tests ----------- */

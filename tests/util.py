@@ -28,8 +28,9 @@ def _dev_copy(torch, bits: np.ndarray, misalign: int, device):
 
 
 def gpu_topk(bits: np.ndarray, k: int, misalign: int = 0, poison: bool = True,
-             stream=None, ws_extra: int = 0):
-    """Fixed-length top-k on cuda:0 through bt_topk_half; returns (value bits, indices)."""
+             stream=None, ws_extra: int = 0, bf16: bool = False):
+    """Fixed-length top-k on cuda:0 through bt_topk_half (bt_topk_bf16 with bf16); returns
+    (value bits, indices)."""
     import torch
 
     import batch_topk_b200 as bt
@@ -37,7 +38,8 @@ def gpu_topk(bits: np.ndarray, k: int, misalign: int = 0, poison: bool = True,
     dev = torch.device("cuda:0")
     seg_num, seg_len = bits.shape
     _buf, x = _dev_copy(torch, bits, misalign, dev)
-    nbytes = bt.batch_topk_half_workspace_size(seg_num, seg_len, k)
+    nbytes = (bt.batch_topk_bf16_workspace_size if bf16 else bt.batch_topk_half_workspace_size)(
+        seg_num, seg_len, k)
     assert nbytes > 0
     ws = torch.empty(nbytes + ws_extra, dtype=torch.uint8, device=dev)
     if poison:
@@ -45,9 +47,10 @@ def gpu_topk(bits: np.ndarray, k: int, misalign: int = 0, poison: bool = True,
     ov = torch.full((seg_num, k), 0x1234, dtype=torch.int16, device=dev)
     oi = torch.full((seg_num, k), -7, dtype=torch.int32, device=dev)
     s = stream or torch.cuda.current_stream(dev)
-    rc = bt.batch_topk_half(x.data_ptr(), seg_num, seg_len, k, ov.data_ptr(), oi.data_ptr(),
-                            ws.data_ptr(), ws.numel(), s.cuda_stream)
-    assert rc == 0, f"bt_topk_half returned {rc}"
+    fn = bt.batch_topk_bf16 if bf16 else bt.batch_topk_half
+    rc = fn(x.data_ptr(), seg_num, seg_len, k, ov.data_ptr(), oi.data_ptr(), ws.data_ptr(),
+            ws.numel(), s.cuda_stream)
+    assert rc == 0, f"top-k returned {rc}"
     s.synchronize()
     flags, _ = bt.workspace_status(ws.data_ptr(), seg_num, s.cuda_stream)
     assert flags == 0, f"device status flags {flags}"
@@ -55,7 +58,8 @@ def gpu_topk(bits: np.ndarray, k: int, misalign: int = 0, poison: bool = True,
 
 
 def gpu_topk_csr(vals: np.ndarray, offsets: np.ndarray, k: int, misalign: int = 0,
-                 max_total_len: int | None = None, check_status: bool = True):
+                 max_total_len: int | None = None, check_status: bool = True,
+                 bf16: bool = False):
     import torch
 
     import batch_topk_b200 as bt
@@ -66,17 +70,18 @@ def gpu_topk_csr(vals: np.ndarray, offsets: np.ndarray, k: int, misalign: int = 
     _buf, x = _dev_copy(torch, vals, misalign, dev)
     d_off = torch.from_numpy(off.astype(np.int32)).to(dev)
     total = int(off[-1] - off[0]) if max_total_len is None else max_total_len
-    nbytes = bt.batch_topk_half_segmented_workspace_size(seg_num, total, k)
+    nbytes = (bt.batch_topk_bf16_segmented_workspace_size if bf16
+              else bt.batch_topk_half_segmented_workspace_size)(seg_num, total, k)
     assert nbytes > 0
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     ws.fill_(0xA5)
     ov = torch.full((seg_num, k), 0x1234, dtype=torch.int16, device=dev)
     oi = torch.full((seg_num, k), -7, dtype=torch.int32, device=dev)
     s = torch.cuda.current_stream(dev)
-    rc = bt.batch_topk_half_segmented(x.data_ptr(), d_off.data_ptr(), seg_num, total, k,
-                                      ov.data_ptr(), oi.data_ptr(), ws.data_ptr(), ws.numel(),
-                                      s.cuda_stream)
-    assert rc == 0, f"bt_topk_half_segmented returned {rc}"
+    fn = bt.batch_topk_bf16_segmented if bf16 else bt.batch_topk_half_segmented
+    rc = fn(x.data_ptr(), d_off.data_ptr(), seg_num, total, k, ov.data_ptr(), oi.data_ptr(),
+            ws.data_ptr(), ws.numel(), s.cuda_stream)
+    assert rc == 0, f"segmented top-k returned {rc}"
     s.synchronize()
     flags, _ = bt.workspace_status(ws.data_ptr(), seg_num, s.cuda_stream)
     if check_status:
