@@ -1,11 +1,14 @@
 """Time the library on the five benchmark configurations (or one of them), one JSON line each.
 
     python -m batch_topk_b200.cases [--config C1|C2|C3|C4|C5|N01] [--k K] [--iters N] [--rows R]
+                                    [--dtype f16|bf16]
 
 Inputs are generated on the device (batch_topk_b200.gen).  Each line gives the median time of
 the streaming kernel alone (CUDA events recorded around it on its stream by the library's
 profiling hook) and of the whole call, and the effective input bandwidth against the
-measured HBM copy peak.  The same command is the target of the ncu summaries under profiles/.
+measured HBM copy peak.  With --dtype bf16 each generated fp16 value is converted to the
+nearest bfloat16 and the bf16 entry points run.  The same command is the target of the ncu
+summaries under profiles/.
 """
 from __future__ import annotations
 
@@ -16,8 +19,10 @@ import os
 import numpy as np
 import torch
 
-from . import batch_topk_half, batch_topk_half_segmented, batch_topk_half_segmented_workspace_size
-from . import batch_topk_half_workspace_size, set_profile_events, workspace_status
+from . import batch_topk_bf16, batch_topk_bf16_segmented, batch_topk_bf16_segmented_workspace_size
+from . import batch_topk_bf16_workspace_size, batch_topk_half, batch_topk_half_segmented
+from . import batch_topk_half_segmented_workspace_size, batch_topk_half_workspace_size
+from . import set_profile_events, workspace_status
 from . import gen
 from . import workloads as wl
 
@@ -49,19 +54,27 @@ def make(config: str, rows: int | None):
     return fn(rows=range(n)), None, cfg.k, n
 
 
-def run(config: str, k: int | None, iters: int, rows: int | None, outputs: bool = False):
+def run(config: str, k: int | None, iters: int, rows: int | None, outputs: bool = False,
+        dtype: str = "f16"):
     """One JSON-ready line; with outputs=True also (input, offsets, values, indices) on the device."""
     x, off, k0, n = make(config, rows)
+    bf16 = dtype == "bf16"
+    if bf16:
+        x = x.view(torch.float16).to(torch.bfloat16).view(torch.int16)
+    fixed, fixed_ws = (batch_topk_bf16, batch_topk_bf16_workspace_size) if bf16 else (
+        batch_topk_half, batch_topk_half_workspace_size)
+    csr, csr_ws = (batch_topk_bf16_segmented, batch_topk_bf16_segmented_workspace_size) if bf16 else (
+        batch_topk_half_segmented, batch_topk_half_segmented_workspace_size)
     k = k or k0
     dev = x.device
     s = torch.cuda.current_stream(dev)
     if off is None:
         seg_len = x.shape[1]
-        nbytes = batch_topk_half_workspace_size(n, seg_len, k)
+        nbytes = fixed_ws(n, seg_len, k)
         total = n * seg_len
     else:
         total = int(off[-1])
-        nbytes = batch_topk_half_segmented_workspace_size(n, total, k)
+        nbytes = csr_ws(n, total, k)
         d_off = torch.from_numpy(off.astype(np.int32)).to(dev)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     ov = torch.empty((n, k), dtype=torch.int16, device=dev)
@@ -69,12 +82,11 @@ def run(config: str, k: int | None, iters: int, rows: int | None, outputs: bool 
 
     def call():
         if off is None:
-            rc = batch_topk_half(x.data_ptr(), n, seg_len, k, ov.data_ptr(), oi.data_ptr(),
-                                 ws.data_ptr(), nbytes, s.cuda_stream)
+            rc = fixed(x.data_ptr(), n, seg_len, k, ov.data_ptr(), oi.data_ptr(), ws.data_ptr(),
+                       nbytes, s.cuda_stream)
         else:
-            rc = batch_topk_half_segmented(x.data_ptr(), d_off.data_ptr(), n, total, k,
-                                           ov.data_ptr(), oi.data_ptr(), ws.data_ptr(), nbytes,
-                                           s.cuda_stream)
+            rc = csr(x.data_ptr(), d_off.data_ptr(), n, total, k, ov.data_ptr(), oi.data_ptr(),
+                     ws.data_ptr(), nbytes, s.cuda_stream)
         if rc != 0:
             raise RuntimeError(f"top-k call returned {rc}")
 
@@ -100,7 +112,7 @@ def run(config: str, k: int | None, iters: int, rows: int | None, outputs: bool 
     flags, _ = workspace_status(ws.data_ptr(), n, s.cuda_stream)
     kt, wt = float(np.median(kern)), float(np.median(whole))
     gbs = total * 2 / kt / 1e6
-    line = {"config": config, "segments": n, "k": k, "values": total, "kernel_us": round(kt * 1e3, 2),
+    line = {"config": config, "dtype": dtype, "segments": n, "k": k, "values": total, "kernel_us": round(kt * 1e3, 2),
             "call_us": round(wt * 1e3, 2), "input_gbs": round(gbs, 1),
             "pct_hbm": round(gbs / hbm_peak(), 4), "status": flags}
     return (line, (x, off, ov, oi)) if outputs else line
@@ -112,12 +124,13 @@ def main():
     ap.add_argument("--k", type=int, action="append", help="k values (C4: default 1, 8, 50, 256)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--rows", type=int, help="first R segments only (C5 defaults to 384)")
+    ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16")
     a = ap.parse_args()
     for config in a.config or ["C1", "C2", "C3", "N01", "C4", "C5"]:
         ks = a.k or (list(wl.C4_K_VALUES) if config == "C4" else [None])
         rows = a.rows or (384 if config == "C5" else None)
         for k in ks:
-            print(json.dumps(run(config, k, a.iters, rows)), flush=True)
+            print(json.dumps(run(config, k, a.iters, rows, dtype=a.dtype)), flush=True)
 
 
 if __name__ == "__main__":

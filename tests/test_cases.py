@@ -24,17 +24,19 @@ def test_cases_help():
 @pytest.mark.gpu
 @pytest.mark.parametrize("config,k,rows", [("C1", None, 4), ("C2", None, 8), ("C3", None, 16),
                                            ("N01", None, 8), ("C4", 256, 12), ("C5", None, 6)])
-def test_cases_line_and_parity(orc, config, k, rows):
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_cases_line_and_parity(orc, config, k, rows, dtype):
     from batch_topk_b200 import cases
 
-    line, (x, off, ov, oi) = cases.run(config, k, 2, rows, outputs=True)
+    line, (x, off, ov, oi) = cases.run(config, k, 2, rows, outputs=True, dtype=dtype)
+    bf16 = dtype == "bf16"
     json.dumps(line)
     assert line["segments"] == rows and line["status"] == 0
     assert line["kernel_us"] > 0 and line["call_us"] >= line["kernel_us"] * 0.5
     xh = x.cpu().numpy().view(np.uint16)
     if off is None:
-        ev, ei = orc.topk(xh, line["k"])
+        ev, ei = orc.topk(xh, line["k"], bf16=bf16)
     else:
-        ev, ei = orc.topk_csr(xh, off, line["k"])
+        ev, ei = orc.topk_csr(xh, off, line["k"], bf16=bf16)
     assert np.array_equal(oi.cpu().numpy(), ei)
     assert np.array_equal(ov.cpu().numpy().view(np.uint16), ev)
