@@ -90,10 +90,6 @@ std::mutex g_mu;
 DeviceInfo g_dev[64];
 cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
 int g_stats = -1;
-int g_part_chunks_env = -1;  // BT_PART_CHUNKS override of the work-part size (0: automatic)
-int g_tail_parts_env = -1;   // BT_TAIL_PARTS: parts per segment in the last wave (0: off)
-int g_tail_segs_env = -1;    // BT_TAIL_SEGS: segments in the last wave (0: one per resident block)
-int g_grid_env = -1;         // BT_GRID: blocks of the streaming kernel (0: automatic)
 int g_steal_env = -1;        // BT_STEAL: 0 turns helping off
 
 // Chunks per work part.  With at least as many segments as resident blocks every block is
@@ -101,7 +97,6 @@ int g_steal_env = -1;        // BT_STEAL: 0 turns helping off
 // first-chunk threshold and a cross-block merge of partial lists.  With fewer segments,
 // about one part per block.
 int choose_part_chunks(long long total_chunks, long long seg_num, long long resident) {
-  if (g_part_chunks_env > 0) return g_part_chunks_env;
   if (seg_num >= resident) return kMaxChunksPerSegment;
   long long u = (total_chunks + resident - 1) / resident;
   if (u < 1) u = 1;
@@ -142,16 +137,8 @@ cudaError_t device_info(DeviceInfo* out) {
       const char* s = std::getenv("BT_STATS");
       g_stats = (s && s[0] == '1') ? 1 : 0;
     }
-    if (g_part_chunks_env < 0) {
-      const char* s = std::getenv("BT_PART_CHUNKS");
-      g_part_chunks_env = s ? std::atoi(s) : 0;
-      s = std::getenv("BT_TAIL_PARTS");
-      g_tail_parts_env = s ? std::atoi(s) : 0;
-      s = std::getenv("BT_TAIL_SEGS");
-      g_tail_segs_env = s ? std::atoi(s) : 0;
-      s = std::getenv("BT_GRID");
-      g_grid_env = s ? std::atoi(s) : 0;
-      s = std::getenv("BT_STEAL");
+    if (g_steal_env < 0) {
+      const char* s = std::getenv("BT_STEAL");
       g_steal_env = s ? std::atoi(s) : 1;
     }
     d.ready = true;
@@ -208,22 +195,12 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, bool b
   long long parts = work_items;  // CSR: an upper bound (every part holds a chunk)
   if (!csr) {
     const long long per = (p.p_max + p.part_chunks - 1) / p.part_chunks;
-    p.tail_seg0 = p.seg_num;
-    p.tail_parts = static_cast<int>(per);
-    if (g_tail_parts_env > per && p.seg_num > 1) {
-      // the last segments in claim order are cut finer, so the final wave ends evenly
-      long long tail = g_tail_segs_env > 0 ? g_tail_segs_env : resident;
-      if (tail > p.seg_num) tail = p.seg_num;
-      p.tail_seg0 = static_cast<int>(p.seg_num - tail);
-      p.tail_parts = g_tail_parts_env < p.p_max ? g_tail_parts_env : p.p_max;
-    }
-    p.parts_total = static_cast<long long>(p.tail_seg0) * per +
-                    static_cast<long long>(p.seg_num - p.tail_seg0) * p.tail_parts;
+    p.parts_total = static_cast<long long>(p.seg_num) * per;
     parts = p.parts_total;
     // Whole segments: claim chunk by chunk and let blocks that run dry help (BT_STEAL=0: off).
     // Only for k <= 128, whose first chunk of a visit is cheap; for larger k a helper's first
     // chunk (select plus exact select) costs more than the chunks it takes over.
-    p.steal = (!big && per == 1 && p.tail_seg0 == p.seg_num && g_steal_env != 0) ? 1 : 0;
+    p.steal = (!big && per == 1 && g_steal_env != 0) ? 1 : 0;
   }
   if (csr) {
     e = launch_setup(csr_prep_kernel, p, 1, 1024, stream);
@@ -232,7 +209,6 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, bool b
   }
   if (e != cudaSuccess) return e;
   long long grid_ll = parts < resident ? (parts > 0 ? parts : 1) : resident;
-  if (g_grid_env > 0 && g_grid_env < grid_ll) grid_ll = g_grid_env;
   const int grid = static_cast<int>(grid_ll);
   p.help_window = p.steal ? (grid < p.seg_num ? grid : p.seg_num) : 0;
   if (g_prof_start) cudaEventRecord(g_prof_start, stream);

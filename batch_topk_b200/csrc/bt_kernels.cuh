@@ -58,8 +58,6 @@ struct TopkParams {
   long long slot_capacity;       // chunk slots in the workspace
   long long parts_total;         // fixed-length: number of work parts
   int part_chunks;               // at most this many chunks per work part
-  int tail_seg0;                 // fixed-length: segments from here on are cut into
-  int tail_parts;                //   tail_parts parts each (the last wave ends evenly)
   int steal;                     // whole segments, chunks claimed one by one, idle blocks help
   int help_window;               // how many of the last-claimed segments idle blocks may help
   uint32_t* chunk_next;          // [seg_num] next unclaimed chunk of each segment (steal)
@@ -230,17 +228,9 @@ __device__ __forceinline__ void decode_part(const TopkParams& p, long long part,
   int seg, j, pps;
   if (!p.offsets) {
     const int per = (p.p_max + p.part_chunks - 1) / p.part_chunks;
-    const long long head = static_cast<long long>(p.tail_seg0) * per;
-    if (part < head) {
-      seg = static_cast<int>(part / per);
-      j = static_cast<int>(part - static_cast<long long>(seg) * per);
-      pps = per;
-    } else {
-      const long long q = part - head;
-      seg = p.tail_seg0 + static_cast<int>(q / p.tail_parts);
-      j = static_cast<int>(q - static_cast<long long>(seg - p.tail_seg0) * p.tail_parts);
-      pps = p.tail_parts;
-    }
+    seg = static_cast<int>(part / per);
+    j = static_cast<int>(part - static_cast<long long>(seg) * per);
+    pps = per;
     *slot0 = static_cast<long long>(seg) * p.p_max;
   } else {
     int lo = 0, hi = p.seg_num;  // part_start[lo] <= part < part_start[hi]
