@@ -96,6 +96,13 @@ __device__ __forceinline__ bool pass_any(const uint4& w, h2t v2) {
 
 // This thread's 8 vectors (tid*8 .. tid*8+7): exact candidate mask of vector j, with the
 // segment-boundary and take-all (no threshold yet) cases.
+// Half e (element order) of a 16-byte vector; e must be a compile-time constant after
+// unrolling, so the word is picked without indexing a register array.
+__device__ __forceinline__ uint32_t vec_half(const uint4& w, int e) {
+  const uint32_t word = e < 2 ? w.x : (e < 4 ? w.y : (e < 6 ? w.z : w.w));
+  return (e & 1) ? (word >> 16) : (word & 0xFFFFu);
+}
+
 template <bool STRICT>
 __device__ __forceinline__ uint32_t vec_mask(const StageInfo& si, const uint8_t* buf, int vi,
                                              h2t v2, bool take_all) {
@@ -260,6 +267,27 @@ __device__ uint32_t buffer_kth_key_block(Scratch<BIG>& sm, uint32_t n, uint32_t 
 // take-all): the reference's two 8-bit digit passes plus ordered tie ranks.  Returns the
 // cutoff key; *S gets this thread's selected elements (bit 8*j+e), *sbase their first output
 // position and *stot the block total (== k).  Rare path.
+
+// Calls f(bits, pos) for every candidate of this thread (bit pos of M, pos = 8 * vector +
+// element; bits = the value's 16-bit pattern).  The thread's vectors are read whole, rotated so a quarter-warp's loads cover all
+// banks; with ORDERED the vectors are visited in index order instead (for tie placement).
+template <bool ORDERED, class F>
+__device__ __forceinline__ void for_each_candidate(const uint8_t* buf, uint64_t M, F&& f) {
+  const int tid = threadIdx.x;
+  const int sw = ORDERED ? 0 : (tid & 7);
+#pragma unroll 1
+  for (int jj = 0; jj < kVecPerThread; ++jj) {
+    const int j = jj ^ sw;
+    const uint32_t m8 = static_cast<uint32_t>(M >> (8 * j)) & 0xFFu;
+    if (m8 == 0) continue;
+    const uint4 w = lds128(buf + (tid * kVecPerThread + j) * 16);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (m8 & (1u << e)) f(vec_half(w, e), 8 * j + e);
+    }
+  }
+}
+
 template <class SM>
 __device__ uint32_t exact_local_select(const TopkParams& p, const StageInfo& si,
                                        const uint8_t* buf, SM& sm, uint32_t K, bool strict,
@@ -277,20 +305,19 @@ __device__ uint32_t exact_local_select(const TopkParams& p, const StageInfo& si,
       M |= static_cast<uint64_t>(m) << (8 * j);
     }
   }
-  const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf) + tid * 64;
   RunHist rh;
-  for (uint64_t m = M; m; m &= m - 1) {
-    rh.add(sm.hist1, desc_key(v16[__ffsll(static_cast<long long>(m)) - 1]) >> 8);
-  }
+  for_each_candidate<false>(buf, M, [&](uint32_t bits, int) {
+    rh.add(sm.hist1, desc_key(bits) >> 8);
+  });
   rh.flush(sm.hist1);
   csync();
   if (tid < 32) warp_find_bin(sm.hist1, 0, p.k, &sm.bin1, &sm.before1);
   csync();
   const uint32_t b1 = static_cast<uint32_t>(sm.bin1);
-  for (uint64_t m = M; m; m &= m - 1) {
-    const uint32_t key = desc_key(v16[__ffsll(static_cast<long long>(m)) - 1]);
+  for_each_candidate<false>(buf, M, [&](uint32_t bits, int) {
+    const uint32_t key = desc_key(bits);
     if ((key >> 8) == b1) rh.add(sm.hist2, key & 0xFFu);
-  }
+  });
   rh.flush(sm.hist2);
   csync();
   if (tid < 32) warp_find_bin(sm.hist2, sm.before1, p.k, &sm.bin2, &sm.before2);
@@ -298,23 +325,22 @@ __device__ uint32_t exact_local_select(const TopkParams& p, const StageInfo& si,
   const uint32_t kstar = (b1 << 8) | static_cast<uint32_t>(sm.bin2);
   const uint32_t need = static_cast<uint32_t>(p.k) - sm.before2;
   uint32_t tcnt = 0;
-  for (uint64_t m = M; m; m &= m - 1) {
-    tcnt += desc_key(v16[__ffsll(static_cast<long long>(m)) - 1]) == kstar ? 1u : 0u;
-  }
+  for_each_candidate<false>(buf, M, [&](uint32_t bits, int) {
+    tcnt += desc_key(bits) == kstar ? 1u : 0u;
+  });
   uint32_t ttot;
   const uint32_t tbase = block_excl_scan<kThreads, true>(tcnt, &ttot, sm.warp_tot);
   uint64_t S = 0;
   uint32_t tr = tbase;
-  for (uint64_t m = M; m; m &= m - 1) {
-    const int pos = __ffsll(static_cast<long long>(m)) - 1;
-    const uint32_t key = desc_key(v16[pos]);
+  for_each_candidate<true>(buf, M, [&](uint32_t bits, int pos) {  // index order: ties by index
+    const uint32_t key = desc_key(bits);
     if (key < kstar) {
       S |= 1ull << pos;
     } else if (key == kstar) {
       if (tr < need) S |= 1ull << pos;
       ++tr;
     }
-  }
+  });
   *sbase_out =
       block_excl_scan<kThreads, true>(static_cast<uint32_t>(__popcll(S)), stot_out, sm.warp_tot);
   *S_out = S;
@@ -333,19 +359,16 @@ __device__ uint32_t exact_local(const TopkParams& p, const StageInfo& si, const 
   uint64_t S;
   uint32_t sbase, stot;
   const uint32_t kstar = exact_local_select(p, si, buf, sm, ss.K, ss.strict, &S, &sbase, &stot);
-  const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf) + tid * 64;
   const bool to_smem = !ss.spilled && ss.nbuf + stot <= static_cast<uint32_t>(Cfg<BIG>::kCacheCap);
   uint32_t* out = p.cand + si.slot * p.cap + sbase;
   const long long e0 = si.cv0 * 8;
   uint32_t r = 0;
-  for (uint64_t m = S; m; m &= m - 1) {
-    const int pos = __ffsll(static_cast<long long>(m)) - 1;
-    const uint32_t lidx = static_cast<uint32_t>(tid * 64 + pos);
-    const uint32_t w = (static_cast<uint32_t>(v16[pos]) << 16) | lidx;
+  for_each_candidate<true>(buf, S, [&](uint32_t bits, int pos) {
+    const uint32_t w = (bits << 16) | static_cast<uint32_t>(tid * 64 + pos);
     out[r] = w;
     if (to_smem) sm.cache[ss.nbuf + sbase + r] = make_composite(w, e0, si.a0);
     ++r;
-  }
+  });
   if (to_smem) ss.nbuf += stot; else ss.spilled = true;
   if (tid == 0) p.chunk_count[si.slot] = stot;
   return kstar;
@@ -353,30 +376,45 @@ __device__ uint32_t exact_local(const TopkParams& p, const StageInfo& si, const 
 
 enum ChunkResult { kChunkDone = 0, kChunkOverflow = 1, kChunkFail = 2 };
 
-// Drops the segment buffer's composites with key > K, keeping their order; returns the new
-// count.  Each thread holds its kCacheCap / kThreads entries in registers across the scan's
-// barriers, so the in-place writes never overtake a read.
+// Keeps, in order, the segment buffer's composites with key < K and the first `need` with
+// key == K, and returns the new count.  The buffer is in index order, so the ties dropped come
+// after `need` earlier ties at K and all keys below K: with K the buffer's k-th key and need =
+// k - (keys below K), they can no longer reach the top k, and exactly k composites remain.
+// Each thread holds its kCacheCap / kThreads entries in registers across the scan's barriers,
+// so the in-place writes never overtake a read.
 template <bool BIG>
-__device__ uint32_t compact_cache(Scratch<BIG>& sm, uint32_t n, uint32_t K) {
+__device__ uint32_t compact_cache(Scratch<BIG>& sm, uint32_t n, uint32_t K, uint32_t need) {
   constexpr int kPer = Cfg<BIG>::kCacheCap / kThreads;
   const uint32_t i0 = threadIdx.x * kPer;
   unsigned long long v[kPer];
-  uint32_t keep = 0;
+  uint32_t lt = 0, eq = 0;
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const uint32_t i = i0 + j;
     v[j] = i < n ? sm.cache[i] : ~0ull;
-    keep += (i < n && static_cast<uint32_t>(v[j] >> 48) <= K) ? 1u : 0u;
+    const uint32_t key = static_cast<uint32_t>(v[j] >> 48);
+    lt += (i < n && key < K) ? 1u : 0u;
+    eq += (i < n && key == K) ? 1u : 0u;
   }
+  // both counts in one scan: each total is at most kCacheCap < 2^16
   uint32_t tot;
-  uint32_t w = block_excl_scan<kThreads, true>(keep, &tot, sm.warp_tot);
+  const uint32_t pre = block_excl_scan<kThreads, true>(lt | (eq << 16), &tot, sm.warp_tot);
+  uint32_t e = pre >> 16;  // ties before this thread's entries
+  uint32_t w = (pre & 0xFFFFu) + (e < need ? e : need);
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const uint32_t i = i0 + j;
-    if (i < n && static_cast<uint32_t>(v[j] >> 48) <= K) sm.cache[w++] = v[j];
+    const uint32_t key = static_cast<uint32_t>(v[j] >> 48);
+    if (i < n && key < K) {
+      sm.cache[w++] = v[j];
+    } else if (i < n && key == K) {
+      if (e < need) sm.cache[w++] = v[j];
+      ++e;
+    }
   }
   csync();
-  return tot;
+  const uint32_t ties = tot >> 16;
+  return (tot & 0xFFFFu) + (ties < need ? ties : need);
 }
 
 // Position of the r-th set bit (r from 0) of a 64-bit mask.
@@ -477,12 +515,12 @@ __device__ int stream_chunk(const TopkParams& p, const StageInfo& si, const uint
   if (BIG && !to_smem && !ss.spilled && ss.nbuf >= static_cast<uint32_t>(p.k)) {
     // make room: the buffer's k-th key is a tighter threshold (k composites at lower
     // indices beat it), and the buffered composites beyond it can go
+    // (kk <= K: every buffered key is at most K)
     const uint32_t kk = buffer_kth_key_block(sm, ss.nbuf, static_cast<uint32_t>(p.k));
-    if (kk < ss.K) {
-      ss.K = kk;
-      ss.strict = true;
-    }
-    ss.nbuf = compact_cache<BIG>(sm, ss.nbuf, ss.K);
+    const uint32_t need = static_cast<uint32_t>(p.k) - sm.before2;  // ties at kk within k
+    ss.K = kk;
+    ss.strict = true;
+    ss.nbuf = compact_cache<BIG>(sm, ss.nbuf, kk, need);
     ss.added = 0;
     to_smem = ss.nbuf + total <= static_cast<uint32_t>(Cfg<BIG>::kCacheCap);
   }

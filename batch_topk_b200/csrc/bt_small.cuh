@@ -175,15 +175,12 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
       const uint32_t kstar = exact_local_select(p, si, buf, sm, K, strict, &S, &sbase, &stot);
       if (!wait_batch_free(sm, nb)) sm.fail = 1u;  // caught at the next barrier
       const int tid = threadIdx.x;
-      const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf) + tid * 64;
       const long long e0 = si.cv0 * 8;
       uint32_t r = 0;
-      for (uint64_t m = S; m; m &= m - 1) {
-        const int pos = __ffsll(static_cast<long long>(m)) - 1;
+      for_each_candidate<true>(buf, S, [&](uint32_t bits, int pos) {
         const uint32_t lidx = static_cast<uint32_t>(tid * 64 + pos);
-        sm.batch[b][sbase + r++] =
-            make_composite((static_cast<uint32_t>(v16[pos]) << 16) | lidx, e0, si.a0);
-      }
+        sm.batch[b][sbase + r++] = make_composite((bits << 16) | lidx, e0, si.a0);
+      });
       K = kstar;
       strict = true;
       n = stot;
