@@ -95,6 +95,24 @@ def test_oracle_bf16_csr_pads_with_bf16_neg_inf(orc):
     assert_exact(gv[2:3], gi[2:3], ev, ei, "csr row 2")
 
 
+def test_bf16_entry_points_keep_the_argument_contract():
+    """Shapes and sizes as the fp16 entry points; bad arguments rejected on the host."""
+    import batch_topk_b200 as bt
+
+    for shape in [(4, 151936, 50), (1, 10, 10), (1024, 262144, 1024)]:
+        assert bt.batch_topk_bf16_workspace_size(*shape) == bt.batch_topk_half_workspace_size(*shape)
+    assert bt.batch_topk_bf16_workspace_size(1, 10, 11) == 0
+    assert bt.batch_topk_bf16_segmented_workspace_size(8, 1000, 50) == \
+        bt.batch_topk_half_segmented_workspace_size(8, 1000, 50)
+    fake = 1 << 20
+    inv = bt.CUDA_ERROR_INVALID_VALUE
+    assert bt.batch_topk_bf16(fake, 0, 100, 5, fake, fake, fake, 1 << 30) == inv   # seg_num
+    assert bt.batch_topk_bf16(fake, 1, 100, 101, fake, fake, fake, 1 << 30) == inv  # k > len
+    assert bt.batch_topk_bf16(0, 1, 100, 5, fake, fake, fake, 1 << 30) == inv      # null input
+    assert bt.batch_topk_bf16(fake, 1, 100, 5, fake, fake, fake, 16) == inv        # workspace
+    assert bt.batch_topk_bf16_segmented(fake, 0, 2, 100, 5, fake, fake, fake, 1 << 30) == inv
+
+
 # ---- GPU: the CUDA path against the checker ------------------------------------------------
 
 SHAPES = [(4, 1000), (16, 32000), (3, 151936), (2, 300001)]
