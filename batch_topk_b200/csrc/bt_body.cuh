@@ -115,7 +115,7 @@ __device__ __forceinline__ uint32_t vec_mask(const StageInfo& si, const uint8_t*
 // Flags (bit j: vector tid*8+j holds a candidate) and the exact candidate count of this
 // thread.  The common case costs one 128-bit smem load, four half2 compares and an OR per
 // vector; exact counting only runs on the rare vectors that pass.
-template <bool STRICT>
+template <bool STRICT, bool DIRECT = false>
 __device__ __forceinline__ uint32_t thread_flags(const StageInfo& si, const uint8_t* buf,
                                                  h2t v2, bool take_all, uint32_t* count) {
   const int tid = threadIdx.x;
@@ -125,7 +125,7 @@ __device__ __forceinline__ uint32_t thread_flags(const StageInfo& si, const uint
                     (si.vhi >= vbase && si.vhi < vbase + kVecPerThread);
   uint32_t flags = 0, cnt = 0;
   if (!edge) {
-    if (vbase + kVecPerThread <= si.nvc) {
+    if (!DIRECT && vbase + kVecPerThread <= si.nvc) {
       // Common case: the maximum of the thread's 64 values (max ignores NaN, which never
       // passes) against the threshold; exact masks only when something passes.
       h2t acc = u32_as_h2(kNaN2);

@@ -32,7 +32,9 @@ __device__ __forceinline__ Counted count_chunk(const StageInfo& si, const uint8_
   const uint32_t vb = key_to_bits(K);
   const h2t v2 = u32_as_h2(vb | (vb << 16));
   Counted c;
-  c.flags = thread_flags<STRICT>(si, buf, v2, take_all, &c.cnt);
+  // A count is needed anyway: masks in one pass, without the maximum pre-test that pays off
+  // only when nothing passes.
+  c.flags = thread_flags<STRICT, true>(si, buf, v2, take_all, &c.cnt);
   uint32_t incl = 0;
   if (__ballot_sync(0xFFFFFFFFu, c.cnt != 0)) {  // warp scan only when something passed
     incl = c.cnt;
