@@ -485,7 +485,7 @@ __device__ int stream_chunk(const TopkParams& p, const StageInfo& si, const uint
   const uint32_t vb = key_to_bits(ss.K);
   const h2t v2 = u32_as_h2(vb | (vb << 16));
   uint32_t cnt;
-  const uint32_t flags = thread_flags<STRICT>(si, buf, v2, take_all, &cnt);
+  const uint32_t flags = thread_flags<STRICT, true>(si, buf, v2, take_all, &cnt);
   uint32_t incl = cnt;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
