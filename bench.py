@@ -15,9 +15,9 @@ value      segments/s over all ranks, inputs resident in HBM, device-timed (CUDA
 e2e        the same metric through the public API from pinned host memory: per step the
            H2D copy of the input and the D2H copy of the values and indices are inside the
            timed region.
-roofline   the streaming kernel (bt::topk_kernel<false>, k <= 128) over the device time per
-           step of the timed region (the kernel plus the unoverlapped part of the set-up
-           kernel launched behind it: an upper bound on the kernel's duration);
+roofline   the streaming kernel (bt::f16::topk_kernel<false>, k <= 128) over the device
+           time per step of the timed region (the kernel plus the unoverlapped part of the
+           set-up kernel launched behind it: an upper bound on the kernel's duration);
            kernel_ms_isolated is the kernel alone, from events the library's profiling hook
            records around it in a second pass (they also expose its launch latency);
            algorithmic bytes = 2 B per input value (the output, 6 B per selected entry, is
@@ -351,7 +351,7 @@ def run_ours(args, rank, world, local_rank):
         "pct_hbm_per_gpu": in_bytes / (ms_per_step / 1e3) / 1e9 / peak,
         "gpu_launches": 2 * args.steps,  # init_kernel + topk_kernel per step
         "roofline": {
-            "bound": "hbm", "kernel": "bt::topk_kernel<false>",
+            "bound": "hbm", "kernel": "bt::f16::topk_kernel<false>",
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
             "algorithmic_bytes_per_launch": in_bytes,
