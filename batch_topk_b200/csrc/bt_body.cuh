@@ -113,8 +113,11 @@ __device__ __forceinline__ uint32_t vec_mask(const StageInfo& si, const uint8_t*
 }
 
 // Flags (bit j: vector tid*8+j holds a candidate) and the exact candidate count of this
-// thread.  The common case costs one 128-bit smem load, four half2 compares and an OR per
-// vector; exact counting only runs on the rare vectors that pass.
+// thread.  Without DIRECT, a pre-test against the maximum of the thread's 64 values (three
+// paired max instructions per vector) decides first, and exact masks follow only on a hit:
+// cheapest when nothing passes.  With DIRECT (a count follows anyway), the masks are built in
+// one pass: each 128-bit smem load is compared (four paired compares), and only the vectors
+// that pass are counted exactly.
 template <bool STRICT, bool DIRECT = false>
 __device__ __forceinline__ uint32_t thread_flags(const StageInfo& si, const uint8_t* buf,
                                                  h2t v2, bool take_all, uint32_t* count) {

@@ -17,7 +17,7 @@ constexpr int kThreads = 256;                         // chunk kernel block size
 constexpr int kWarps = kThreads / 32;
 constexpr int kVecPerThread = 8;                      // 16-byte vectors per thread
 constexpr int kVecPerChunk = kThreads * kVecPerThread;  // 2048 vectors
-constexpr int kChunkElems = kVecPerChunk * 8;         // 16384 fp16 values
+constexpr int kChunkElems = kVecPerChunk * 8;         // 16384 16-bit values
 constexpr int kStageBytes = kVecPerChunk * 16;        // 32 KiB per pipeline stage
 constexpr int kStages = 3;
 constexpr int kMaxK = 1024;
