@@ -210,3 +210,58 @@ def test_torch_api_matches_torch_topk():
     tv, _ = torch.topk(x.float(), 50, dim=1)
     assert torch.equal(v.float(), tv)
     assert torch.equal(torch.gather(x, 1, i.long()), v)
+
+
+def test_back_to_back_calls_without_sync(orc):
+    """Calls queued back to back on one stream, sharing a workspace, with kernels that rewrite
+    the input in between and no host synchronisation until the end.  Each call's set-up kernel
+    is launched early behind the previous kernel and waits for it: every result must match the
+    checker on the input as it was at that call (snapshots are taken in stream order)."""
+    import torch
+
+    import batch_topk_b200 as bt
+
+    dev = torch.device("cuda:0")
+    s = torch.cuda.current_stream(dev)
+    rng = np.random.default_rng(21)
+    seg_num, seg_len = 64, 40000
+    xt = torch.from_numpy(rng.standard_normal((seg_num, seg_len)).astype(np.float16)).to(dev)
+    off = np.linspace(0, seg_num * seg_len, 9).astype(np.int64)  # 8 CSR segments, same buffer
+    d_off = torch.from_numpy(off.astype(np.int32)).to(dev)
+    total = seg_num * seg_len
+    plan = [("fixed", 50), ("neg", 0), ("fixed", 1024), ("csr", 50), ("scale", 0), ("fixed", 8),
+            ("csr", 300), ("fixed", 50)]
+    need = max(bt.batch_topk_half_workspace_size(seg_num, seg_len, 1024),
+               bt.batch_topk_half_segmented_workspace_size(8, total, 300))
+    ws = torch.empty(need, dtype=torch.uint8, device=dev)
+    ws.fill_(0xA5)
+    runs = []
+    for op, k in plan:
+        if op == "neg":
+            xt.neg_()
+            continue
+        if op == "scale":
+            xt.mul_(0.5)
+            continue
+        snap = xt.clone()
+        rows = seg_num if op == "fixed" else 8
+        ov = torch.empty((rows, k), dtype=torch.int16, device=dev)
+        oi = torch.empty((rows, k), dtype=torch.int32, device=dev)
+        if op == "fixed":
+            rc = bt.batch_topk_half(xt.data_ptr(), seg_num, seg_len, k, ov.data_ptr(),
+                                    oi.data_ptr(), ws.data_ptr(), ws.numel(), s.cuda_stream)
+        else:
+            rc = bt.batch_topk_half_segmented(xt.data_ptr(), d_off.data_ptr(), 8, total, k,
+                                              ov.data_ptr(), oi.data_ptr(), ws.data_ptr(),
+                                              ws.numel(), s.cuda_stream)
+        assert rc == 0
+        runs.append((op, k, snap, ov, oi))
+    torch.cuda.synchronize(dev)
+    for n, (op, k, snap, ov, oi) in enumerate(runs):
+        bits = snap.cpu().numpy().view(np.uint16)
+        if op == "fixed":
+            exp_v, exp_i = orc.topk(bits, k)
+        else:
+            exp_v, exp_i = orc.topk_csr(bits.reshape(-1), off, k)
+        assert_exact(ov.cpu().numpy().view(np.uint16), oi.cpu().numpy(), exp_v, exp_i,
+                     f"call {n} ({op}, k={k})")
