@@ -78,8 +78,9 @@ def csr_local(offsets: np.ndarray, s0: int, s1: int) -> tuple[np.ndarray, int, i
 Runner = Callable[[int, int, np.ndarray, "np.ndarray | None", int], tuple]
 
 
-def device_runner(rank: int, device: int, x: np.ndarray, offsets, k: int):
-    """Top-k of one shard on `device` through the library, from and back to host memory."""
+def device_runner(rank: int, device: int, x: np.ndarray, offsets, k: int, bf16: bool = False):
+    """Top-k of one shard on `device` through the library, from and back to host memory
+    (fp16 bits, or bf16 bits with bf16)."""
     import torch
 
     from . import torch_api
@@ -89,11 +90,12 @@ def device_runner(rank: int, device: int, x: np.ndarray, offsets, k: int):
         stream = torch.cuda.Stream(dev)
         if x.size == 0:
             rows = 0 if offsets is None else len(offsets) - 1
-            return (np.full((rows, k), 0xFC00, np.uint16), np.full((rows, k), -1, np.int32))
+            pad = 0xFF80 if bf16 else 0xFC00  # -inf
+            return (np.full((rows, k), pad, np.uint16), np.full((rows, k), -1, np.int32))
         xh = torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).pin_memory()
         ws = torch_api.Workspace(dev)
         with torch.cuda.stream(stream):
-            xd = xh.to(dev, non_blocking=True).view(torch.float16)
+            xd = xh.to(dev, non_blocking=True).view(torch.bfloat16 if bf16 else torch.float16)
             if offsets is None:
                 v, i = torch_api.topk(xd, k, workspace=ws, stream=stream)
             else:
@@ -106,13 +108,14 @@ def device_runner(rank: int, device: int, x: np.ndarray, offsets, k: int):
 
 
 def topk_multi_gpu(x: np.ndarray, k: int, devices: Sequence[int], offsets=None,
-                   runner: Runner | None = None):
+                   runner: Runner | None = None, bf16: bool = False):
     """Top-k of a host batch sharded by segment over `devices` (one host thread each).
 
-    x is [seg_num, seg_len] uint16 fp16 bits, or 1-D with CSR `offsets` [seg_num+1].  Returns
-    (values uint16 [seg_num, k], indices int32 [seg_num, k]).  If any shard fails, every
-    thread is joined first and then ShardFailure names the lowest failing rank."""
-    run = runner or device_runner
+    x is [seg_num, seg_len] uint16 fp16 bits (bf16 bits with bf16), or 1-D with CSR
+    `offsets` [seg_num+1].  Returns (values uint16 [seg_num, k], indices int32 [seg_num, k]).
+    If any shard fails, every thread is joined first and then ShardFailure names the lowest
+    failing rank.  A custom runner gets (rank, device, shard, offsets, k)."""
+    run = runner or (lambda r, d, xs, o, kk: device_runner(r, d, xs, o, kk, bf16=bf16))
     world = len(devices)
     if world == 0:
         raise ValueError("no devices")

@@ -189,3 +189,18 @@ def test_device_shards_on_one_gpu_equal_single(orc):
     ev, ei = orc.topk_csr(xc, off, 256)
     v, i = shard.topk_multi_gpu(xc, 256, devices=[0, 0, 0], offsets=off)
     assert np.array_equal(v, ev) and np.array_equal(i, ei)
+
+
+@pytest.mark.gpu
+def test_device_shards_bf16(orc):
+    """bf16 rows and a CSR batch with an empty segment, sharded on cuda:0."""
+    rng = np.random.default_rng(4)
+    x = (rng.standard_normal((6, 30000)).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    ev, ei = orc.topk(x, 50, bf16=True)
+    v, i = shard.topk_multi_gpu(x, 50, devices=[0, 0], bf16=True)
+    assert np.array_equal(v, ev) and np.array_equal(i, ei)
+    off = np.array([0, 0, 1000, 1000, 40000, 90000], np.int64)
+    xc = (rng.standard_normal(90000).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    ev, ei = orc.topk_csr(xc, off, 64, bf16=True)
+    v, i = shard.topk_multi_gpu(xc, 64, devices=[0, 0, 0], offsets=off, bf16=True)
+    assert np.array_equal(v, ev) and np.array_equal(i, ei)
