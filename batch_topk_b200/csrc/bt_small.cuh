@@ -231,6 +231,7 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
   uint32_t guess = kNoThreshold;  // the previous part's first-chunk threshold
   uint32_t tight = kNoThreshold;  // the previous part's final threshold
   bool tight_hot = true;
+  bool second_hot = true;  // the test on a part's second chunk found it quiet last time it ran
   long long nb = 0;  // batches sent
   int st = 0, par = 0;
   uint32_t ph = 0;   // full-barrier phase parity of stage st
@@ -258,7 +259,12 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
       // The chunk right after the part's first one is tried too: once the first chunk has
       // certified a strict threshold, tie-heavy rows have nothing left to pass.
       bool done = false;
-      if (ss.strict && ss.K < kNoThreshold && (ss.quiet || ss.mycnt == 1)) {
+      // After a miss on a second chunk the next part skips that test once (rows whose first
+      // threshold is loose rarely have a quiet second chunk; tie-heavy rows always do).
+      const bool second = ss.mycnt == 1 && !ss.quiet;
+      bool try_second = second && second_hot;
+      if (second && !second_hot) second_hot = true;  // skipped once: the next part tries again
+      if (ss.strict && ss.K < kNoThreshold && (ss.quiet || try_second)) {
         const bool last = si.last != 0;  // read before the barrier
         const uint32_t vb = key_to_bits(ss.K);
         uint32_t cnt;
@@ -285,6 +291,7 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
           ++nb;
         }
       }
+      if (try_second && !done && ss.strict && ss.K < kNoThreshold) second_hot = false;
       if (!done) {
         const long long nb0 = nb;
         const int r = small_chunk(p, si, buf, sm, ss, par, &nb, &guess, &tight, &tight_hot);
