@@ -33,6 +33,31 @@ def test_fake_kernel_rejects_wrong_dtype():
         torch.ops.batch_topk_b200.topk(torch.empty((2, 10), dtype=torch.float32, device="cuda"), 3)
 
 
+def test_fake_kernels_keep_bfloat16():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        x = torch.empty((3, 500), dtype=torch.bfloat16, device="cuda")
+        v, i = torch.ops.batch_topk_b200.topk(x, 7)
+        assert v.shape == (3, 7) and v.dtype == torch.bfloat16 and i.dtype == torch.int32
+        off = torch.empty((4,), dtype=torch.int32, device="cuda")
+        v, i = torch.ops.batch_topk_b200.topk_segmented(torch.empty((900,), dtype=torch.bfloat16,
+                                                                    device="cuda"), off, 5)
+        assert v.shape == (3, 5) and v.dtype == torch.bfloat16
+
+
+def test_eager_calls_reject_host_tensors_and_other_dtypes():
+    from batch_topk_b200 import torch_api
+
+    with pytest.raises(ValueError):
+        torch_api.topk(torch.zeros((2, 10), dtype=torch.float16), 3)       # host memory
+    with pytest.raises(ValueError):
+        torch_api.topk(torch.zeros((2, 10), dtype=torch.float32), 3)       # not 16-bit
+    with pytest.raises(ValueError):
+        torch_api.topk_segmented(torch.zeros((10,), dtype=torch.bfloat16),
+                                 torch.zeros((3,), dtype=torch.int32), 2)
+
+
 @pytest.mark.gpu
 def test_operator_matches_oracle_and_torch_topk(orc):
     x = wl.gen_c2(rows=slice(0, 16))
