@@ -20,8 +20,12 @@ MAX_K = 1024
 MAX_SEG_LEN = 1 << 26
 NOALLOC_SCRATCH_BYTES = 32 << 20  # BT_NOALLOC_SCRATCH_BYTES
 
+STATUS_WAIT_TIMEOUT = 1
+STATUS_BAD_OFFSETS = 2
+STATUS_SEGMENT_TOO_LONG = 4
+STATUS_CERTIFY_FAILED = 8
 STATUS_FLAGS = {
-    1: "bulk-copy wait timed out",
+    1: "a bounded device wait (bulk copy or hand-off) timed out",
     2: "CSR offsets decreasing or beyond max_total_len",
     4: "segment longer than the supported maximum",
     8: "candidate certification failed",
@@ -33,6 +37,16 @@ class BatchTopkError(RuntimeError):
         self.code = code
         msg = _lib.load().bt_error_string(code).decode()
         super().__init__(f"{what}: error {code}: {msg}" if what else f"error {code}: {msg}")
+
+
+class DeviceStatusError(RuntimeError):
+    """A device-side check of a call failed (its workspace status word holds STATUS_* flags)."""
+
+    def __init__(self, flags: int, what: str = ""):
+        self.flags = flags
+        names = "; ".join(v for b, v in STATUS_FLAGS.items() if flags & b)
+        super().__init__(f"{what}: device status {flags:#x} ({names})" if what
+                         else f"device status {flags:#x} ({names})")
 
 
 def batch_topk_half(d_input: int, seg_num: int, seg_len: int, k: int, d_output_values: int,
@@ -108,6 +122,22 @@ def workspace_status(d_workspace: int, seg_num: int = 0, stream: int = 0):
     if rc < 0:
         raise BatchTopkError(-rc, "bt_workspace_status")
     return rc, tuple(int(v) for v in stats)
+
+
+def noalloc_status(stream: int = 0):
+    """workspace_status for batch_topk_half_noalloc: the status of the last no-alloc call on
+    the current device, read from the library's fixed scratch array (allocates nothing)."""
+    stats = (C.c_uint * 6)()
+    rc = _lib.load().bt_noalloc_status(stream, C.byref(stats))
+    if rc < 0:
+        raise BatchTopkError(-rc, "bt_noalloc_status")
+    return rc, tuple(int(v) for v in stats)
+
+
+def set_handoff_wait_tries(tries: int | None) -> None:
+    """Failure-path test hook: tries of each consumer <-> merger hand-off wait of later calls
+    (0: fail at once, so the call ends with STATUS_WAIT_TIMEOUT; None: the default)."""
+    _lib.load().bt_set_handoff_wait_tries(-1 if tries is None else int(tries))
 
 
 def set_profile_events(ev_start: int | None, ev_stop: int | None) -> None:

@@ -22,6 +22,8 @@ EXPORTED = (
     "bt_topk_bf16_segmented",
     "bt_topk_bf16_segmented_workspace_size",
     "bt_workspace_status",
+    "bt_noalloc_status",
+    "bt_set_handoff_wait_tries",
     "bt_set_profile_events",
     "bt_device_info",
     "bt_error_string",
@@ -67,6 +69,10 @@ def load() -> C.CDLL:
         lib.bt_topk_bf16_segmented_workspace_size.restype = sz
         lib.bt_workspace_status.argtypes = [vp, i32, vp, C.POINTER(C.c_uint * 6)]
         lib.bt_workspace_status.restype = i32
+        lib.bt_noalloc_status.argtypes = [vp, C.POINTER(C.c_uint * 6)]
+        lib.bt_noalloc_status.restype = i32
+        lib.bt_set_handoff_wait_tries.argtypes = [i32]
+        lib.bt_set_handoff_wait_tries.restype = None
         lib.bt_set_profile_events.argtypes = [vp, vp]
         lib.bt_set_profile_events.restype = None
         lib.bt_error_string.argtypes = [i32]

@@ -91,6 +91,7 @@ DeviceInfo g_dev[64];
 cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
 int g_stats = -1;
 int g_steal_env = -1;        // BT_STEAL: 0 turns helping off
+uint32_t g_handoff_tries = kWaitCap;  // bt_set_handoff_wait_tries (failure-path tests)
 
 // Chunks per work part.  With at least as many segments as resident blocks every block is
 // busy with whole segments, and a segment is never split: each extra part costs its own
@@ -189,6 +190,10 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, bool b
   cudaError_t e = device_info(&di);
   if (e != cudaSuccess) return e;
   p.stats = g_stats > 0 ? 1 : 0;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    p.handoff_tries = g_handoff_tries;
+  }
   const bool big = p.k > Cfg<false>::kSelCap;
   const long long resident = static_cast<long long>(di.sms) * di.blocks_per_sm[big ? 1 : 0];
   p.part_chunks = choose_part_chunks(work_items, p.seg_num, resident);
@@ -290,6 +295,7 @@ int topk_csr(const void* d_input, const int* d_offsets, int seg_num, long long m
   p.seg_len = 0;
   p.offsets = d_offsets;
   p.p_max = 0;
+  p.max_total_len = max_total_len;
   return launch_pipeline(p, true, slots, bf16, static_cast<cudaStream_t>(stream));
 }
 
@@ -409,6 +415,19 @@ int bt_workspace_status(const void* d_workspace, int seg_num, void* stream, unsi
     for (int i = 0; i < BT_STATS_WORDS; ++i) stats[i] = words[1 + i];
   }
   return static_cast<int>(words[0]);
+}
+
+int bt_noalloc_status(void* stream, unsigned* stats) {
+  void* scratch = nullptr;
+  const cudaError_t e = bt::noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return -static_cast<int>(e);
+  // the status words open the scratch, as they open every workspace (make_layout)
+  return bt_workspace_status(scratch, 0, stream, stats);
+}
+
+void bt_set_handoff_wait_tries(int tries) {
+  std::lock_guard<std::mutex> lock(bt::g_mu);
+  bt::g_handoff_tries = tries < 0 ? bt::kWaitCap : static_cast<uint32_t>(tries);
 }
 
 void bt_set_profile_events(void* ev_start, void* ev_stop) {

@@ -11,10 +11,61 @@ namespace BT_ELEM_NS {
 
 #include "bt_elem.cuh"
 
+// k-th smallest of the block's group keys, nw packed words (two 16-bit keys each) per thread
+// held in kw (0xFFFF: a NaN maximum, never counted), or kNoThreshold when fewer than k keys are
+// numeric: two 8-bit digit histograms over the block (per-thread runs aggregated before the
+// shared atomics).  The histograms are zero on entry and left zero.
+template <class SM>
+__device__ __forceinline__ uint32_t block_kth_keys(const uint32_t (&kw)[4], int nw, uint32_t k,
+                                                   SM& sm) {
+  const int tid = threadIdx.x;
+  RunHist rh;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (i < nw) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t key = (kw[i] >> (16 * h)) & 0xFFFFu;
+        if (key != 0xFFFFu) rh.add(sm.hist1, key >> 8);
+      }
+    }
+  }
+  rh.flush(sm.hist1);
+  csync();
+  if (tid < 32) warp_find_bin(sm.hist1, 0, k, &sm.bin1, &sm.before1);
+  csync();
+  const int b1 = sm.bin1;
+  uint32_t result = kNoThreshold;
+  if (b1 < 256) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (i < nw) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t key = (kw[i] >> (16 * h)) & 0xFFFFu;
+          if (key != 0xFFFFu && (key >> 8) == static_cast<uint32_t>(b1)) {
+            rh.add(sm.hist2, key & 0xFFu);
+          }
+        }
+      }
+    }
+    rh.flush(sm.hist2);
+    csync();
+    if (tid < 32) warp_find_bin(sm.hist2, sm.before1, k, &sm.bin2, &sm.before2);
+    csync();
+    result = (static_cast<uint32_t>(b1) << 8) | static_cast<uint32_t>(sm.bin2);
+  }
+  sm.hist1[tid] = 0;
+  sm.hist2[tid] = 0;
+  csync();
+  return result;
+}
+
 // k-th best group maximum of the chunk (descending key), or kNoThreshold when the chunk has
 // fewer than k non-NaN maxima.  Each maximum is a distinct element, so at least k elements
-// of the chunk are >= it and every member of the segment's top-k is >= it.  Two barriers:
-// the group keys go to shared memory, warp 0 selects, and the result is broadcast.
+// of the chunk are >= it and every member of the segment's top-k is >= it.  k <= 128: two
+// barriers (the group keys go to shared memory, warp 0 selects, and the result is broadcast);
+// larger k: the block-wide digit select above over 1024 or 2048 group keys.
 template <bool BIG>
 __device__ uint32_t chunk_select(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
                                  Scratch<BIG>& sm) {
@@ -62,18 +113,23 @@ __device__ uint32_t chunk_select(const TopkParams& p, const StageInfo& si, const
       nw = 1;
     }
   }
-  for (int i = 0; i < nw; ++i) sm.gkeys[i * kThreads + tid] = kw[i];
-  csync();
-  if (tid < 32) {  // lane l owns words [l * per, (l + 1) * per) of the nw * kThreads words
-    const int per = nw * kThreads / 32;
-    const uint32_t K = per == 8 ? kth_keys16(sm.gkeys + lane * 8, static_cast<uint32_t>(p.k))
-                                : kth_packed_keys(sm.gkeys + lane * per, per,
-                                                  static_cast<uint32_t>(p.k));
-    if (lane == 0) sm.bcast[3] = K;
-    if (lane == 0 && p.stats) atomicAdd(&p.status[3], 1u);
+  if constexpr (BIG) {
+    if (tid == 0 && p.stats) atomicAdd(&p.status[3], 1u);
+    return block_kth_keys(kw, nw, static_cast<uint32_t>(p.k), sm);
+  } else {
+    for (int i = 0; i < nw; ++i) sm.gkeys[i * kThreads + tid] = kw[i];
+    csync();
+    if (tid < 32) {  // lane l owns words [l * per, (l + 1) * per) of the nw * kThreads words
+      const int per = nw * kThreads / 32;
+      const uint32_t K = per == 8 ? kth_keys16(sm.gkeys + lane * 8, static_cast<uint32_t>(p.k))
+                                  : kth_packed_keys(sm.gkeys + lane * per, per,
+                                                    static_cast<uint32_t>(p.k));
+      if (lane == 0) sm.bcast[3] = K;
+      if (lane == 0 && p.stats) atomicAdd(&p.status[3], 1u);
+    }
+    csync();
+    return sm.bcast[3];  // 0xFFFF: no certified threshold (fewer than k non-NaN maxima)
   }
-  csync();
-  return sm.bcast[3];  // 0xFFFF: no certified threshold (fewer than k non-NaN maxima)
 }
 
 // Threshold test of one 16-byte vector: 8-bit element mask (bit e = element e) of values
@@ -181,18 +237,16 @@ __device__ __forceinline__ unsigned long long make_composite(uint32_t word, long
          (static_cast<unsigned long long>(idx) << 16) | raw;
 }
 
-// Writes this thread's candidates (flagged vectors, index order) at [base, ...) of the
-// chunk's slot, and as (key, index, bits) composites at nbuf + base of the segment's
-// shared-memory buffer when to_smem.
+// Writes this thread's candidates (flagged vectors, index order) as (key, index, bits)
+// composites at sm.cache[nbuf + base ...].
 template <bool STRICT, bool BIG>
-__device__ __forceinline__ void write_flagged(const TopkParams& p, const StageInfo& si,
-                                              const uint8_t* buf, uint32_t flags, h2t v2,
-                                              bool take_all, uint32_t base, Scratch<BIG>& sm,
-                                              uint32_t nbuf, bool to_smem) {
+__device__ __forceinline__ void write_flagged(const StageInfo& si, const uint8_t* buf,
+                                              uint32_t flags, h2t v2, bool take_all,
+                                              uint32_t base, Scratch<BIG>& sm, uint32_t nbuf) {
   const int tid = threadIdx.x;
-  uint32_t* out = p.cand + si.slot * p.cap + base;
   const long long e0 = si.cv0 * 8;
   const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf);
+  unsigned long long* out = sm.cache + nbuf + base;
   uint32_t r = 0;
   while (flags) {
     const int j = __ffs(flags) - 1;
@@ -203,10 +257,7 @@ __device__ __forceinline__ void write_flagged(const TopkParams& p, const StageIn
       const int e = __ffs(m) - 1;
       m &= m - 1;
       const uint32_t lidx = static_cast<uint32_t>(vi * 8 + e);
-      const uint32_t w = (static_cast<uint32_t>(v16[lidx]) << 16) | lidx;
-      out[r] = w;
-      if (to_smem) sm.cache[nbuf + base + r] = make_composite(w, e0, si.a0);
-      ++r;
+      out[r++] = make_composite((static_cast<uint32_t>(v16[lidx]) << 16) | lidx, e0, si.a0);
     }
   }
 }
@@ -353,30 +404,6 @@ __device__ uint32_t exact_local_select(const TopkParams& p, const StageInfo& si,
   return kstar;
 }
 
-// Large-k path: exact local select, written to the chunk's global slot and the segment's
-// shared-memory buffer.
-template <bool BIG>
-__device__ uint32_t exact_local(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
-                                Scratch<BIG>& sm, SegState& ss) {
-  const int tid = threadIdx.x;
-  uint64_t S;
-  uint32_t sbase, stot;
-  const uint32_t kstar = exact_local_select(p, si, buf, sm, ss.K, ss.strict, &S, &sbase, &stot);
-  const bool to_smem = !ss.spilled && ss.nbuf + stot <= static_cast<uint32_t>(Cfg<BIG>::kCacheCap);
-  uint32_t* out = p.cand + si.slot * p.cap + sbase;
-  const long long e0 = si.cv0 * 8;
-  uint32_t r = 0;
-  for_each_candidate<true>(buf, S, [&](uint32_t bits, int pos) {
-    const uint32_t w = (bits << 16) | static_cast<uint32_t>(tid * 64 + pos);
-    out[r] = w;
-    if (to_smem) sm.cache[ss.nbuf + sbase + r] = make_composite(w, e0, si.a0);
-    ++r;
-  });
-  if (to_smem) ss.nbuf += stot; else ss.spilled = true;
-  if (tid == 0) p.chunk_count[si.slot] = stot;
-  return kstar;
-}
-
 enum ChunkResult { kChunkDone = 0, kChunkOverflow = 1, kChunkFail = 2 };
 
 // Keeps, in order, the segment buffer's composites with key < K and the first `need` with
@@ -445,9 +472,9 @@ __device__ __forceinline__ int select_bit64(unsigned long long m, uint32_t r) {
 // mask).  For clustered candidates (a sorted row's top values sit in a few threads) this keeps
 // the block from waiting on a few serial writers.
 template <bool STRICT, bool BIG>
-__device__ void write_balanced(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
-                               uint32_t flags, h2t v2, bool take_all, uint32_t base,
-                               uint32_t total, Scratch<BIG>& sm, uint32_t nbuf, bool to_smem) {
+__device__ void write_balanced(const StageInfo& si, const uint8_t* buf, uint32_t flags, h2t v2,
+                               bool take_all, uint32_t base, uint32_t total, Scratch<BIG>& sm,
+                               uint32_t nbuf) {
   const int tid = threadIdx.x;
   unsigned long long M = 0;
   for (uint32_t f = flags; f; f &= f - 1) {
@@ -458,7 +485,6 @@ __device__ void write_balanced(const TopkParams& p, const StageInfo& si, const u
   sm.tmask[tid] = M;
   sm.tbase[tid] = base;
   csync();
-  uint32_t* out = p.cand + si.slot * p.cap;
   const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf);
   const long long e0 = si.cv0 * 8;
   for (uint32_t i = tid; i < total; i += kThreads) {
@@ -469,113 +495,9 @@ __device__ void write_balanced(const TopkParams& p, const StageInfo& si, const u
     }
     const int pos = select_bit64(sm.tmask[lo], i - sm.tbase[lo]);
     const uint32_t lidx = static_cast<uint32_t>(lo * 64 + pos);
-    const uint32_t w = (static_cast<uint32_t>(v16[lidx]) << 16) | lidx;
-    out[i] = w;
-    if (to_smem) sm.cache[nbuf + i] = make_composite(w, e0, si.a0);
+    sm.cache[nbuf + i] = make_composite((static_cast<uint32_t>(v16[lidx]) << 16) | lidx, e0, si.a0);
   }
   csync();  // tmask / tbase are free again
-}
-
-// Counts the chunk's candidates under (ss.K, STRICT) with one barrier, then writes them in
-// index order.  `par` selects the double-buffered warp-count slots.
-template <bool STRICT, bool BIG>
-__device__ int stream_chunk(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
-                            Scratch<BIG>& sm, SegState& ss, int par) {
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  const bool take_all = ss.K == kNoThreshold;
-  const uint32_t vb = key_to_bits(ss.K);
-  const h2t v2 = u32_as_h2(vb | (vb << 16));
-  uint32_t cnt;
-  const uint32_t flags = thread_flags<STRICT, true>(si, buf, v2, take_all, &cnt);
-  uint32_t incl = cnt;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-    if (lane >= o) incl += y;
-  }
-  if (lane == 31) sm.wcnt[par][warp] = incl;
-  csync();
-  if (sm.fail) return kChunkFail;
-  uint32_t total = 0, wpre = 0;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    const uint32_t t = sm.wcnt[par][w];
-    wpre += w < warp ? t : 0u;
-    total += t;
-  }
-  if (total == 0) {
-    if (tid == 0) {
-      p.chunk_count[si.slot] = 0;
-      if (p.stats) atomicAdd(&p.status[2], 1u);
-    }
-    return kChunkDone;
-  }
-  if (total > static_cast<uint32_t>(p.cap)) return kChunkOverflow;
-  const uint32_t base = wpre + incl - cnt;
-  bool to_smem = !ss.spilled && ss.nbuf + total <= static_cast<uint32_t>(Cfg<BIG>::kCacheCap);
-  if (BIG && !to_smem && !ss.spilled && ss.nbuf >= static_cast<uint32_t>(p.k)) {
-    // make room: the buffer's k-th key is a tighter threshold (k composites at lower
-    // indices beat it), and the buffered composites beyond it can go
-    // (kk <= K: every buffered key is at most K)
-    const uint32_t kk = buffer_kth_key_block(sm, ss.nbuf, static_cast<uint32_t>(p.k));
-    const uint32_t need = static_cast<uint32_t>(p.k) - sm.before2;  // ties at kk within k
-    ss.K = kk;
-    ss.strict = true;
-    ss.nbuf = compact_cache<BIG>(sm, ss.nbuf, kk, need);
-    ss.added = 0;
-    to_smem = ss.nbuf + total <= static_cast<uint32_t>(Cfg<BIG>::kCacheCap);
-  }
-  if (BIG && total >= 512) {
-    write_balanced<STRICT, BIG>(p, si, buf, flags, v2, take_all, base, total, sm, ss.nbuf, to_smem);
-  } else if (flags) {
-    write_flagged<STRICT, BIG>(p, si, buf, flags, v2, take_all, base, sm, ss.nbuf, to_smem);
-  }
-  if (tid == 0) p.chunk_count[si.slot] = total;
-  if (to_smem) {
-    ss.nbuf += total;
-    ss.added += total;
-  } else {
-    ss.spilled = true;
-  }
-  if (!take_all) {
-    // >= k values with key <= K are now written (certified by this segment's own select or
-    // exact pass, earlier in index order): later chunks only need key < K.  Once k more
-    // candidates have arrived, tighten K to the exact k-th best of the buffer.
-    ss.strict = true;
-    // once k more candidates have arrived, tighten K to the buffer's k-th key (k composites at
-    // lower indices beat it, so it is a strict threshold)
-    if (ss.added >= static_cast<uint32_t>(p.k) && !ss.spilled) {
-      csync();
-      const uint32_t kk = buffer_kth_key_block(sm, ss.nbuf, static_cast<uint32_t>(p.k));
-      if (kk < ss.K) ss.K = kk;
-      ss.added = 0;
-    }
-  }
-  return kChunkDone;
-}
-
-// First chunk of a segment (or one after an uncertified chunk): select a threshold, stream,
-// and fall back to the exact local select when too many values pass.
-template <bool BIG>
-__device__ __forceinline__ int first_chunk(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
-                           Scratch<BIG>& sm, SegState& ss, int par, bool* adopted = nullptr) {
-  const uint32_t kc = chunk_select(p, si, buf, sm);
-  if (adopted) *adopted = kc < ss.K;
-  if (kc < ss.K) {
-    ss.K = kc;
-    ss.strict = false;
-  }
-  int r = ss.strict ? stream_chunk<true, BIG>(p, si, buf, sm, ss, par)
-                    : stream_chunk<false, BIG>(p, si, buf, sm, ss, par);
-  if (r == kChunkOverflow) {
-    ss.K = exact_local(p, si, buf, sm, ss);
-    ss.strict = true;
-    ss.added = 0;
-    r = kChunkDone;
-  }
-  return r;
 }
 
 // ---- consumer: segment merge -----------------------------------------------------------
@@ -585,23 +507,6 @@ __device__ __forceinline__ int first_chunk(const TopkParams& p, const StageInfo&
 struct CacheSrc {
   const unsigned long long* cache;
   __device__ __forceinline__ unsigned long long get(uint32_t i) const { return cache[i]; }
-};
-
-struct GlobalSrc {
-  const TopkParams* p;
-  const uint32_t* coff;  // P + 1 prefix entries (shared or global memory)
-  int P;
-  long long slot0, v0, a0;
-  int chunk_vecs;
-  __device__ __forceinline__ unsigned long long get(uint32_t i) const {
-    int lo = 0, hi = P;  // largest c with coff[c] <= i
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (coff[mid] <= i) lo = mid; else hi = mid;
-    }
-    const uint32_t w = __ldcg(&p->cand[(slot0 + lo) * p->cap + (i - coff[lo])]);
-    return make_composite(w, (v0 + static_cast<long long>(lo) * chunk_vecs) * 8, a0);
-  }
 };
 
 // Each of the n candidates with key <= kf takes the output slot given by its rank in
@@ -769,221 +674,8 @@ __device__ __forceinline__ void emit_from_cache(const TopkParams& p, Scratch<BIG
   }
 }
 
-// Merges segment ss.s from the chunk lists in global memory (split or overflowing segments).
-template <bool BIG>
-__device__ void merge_from_global(const TopkParams& p, const SegState& ss, uint32_t kf,
-                                  Scratch<BIG>& sm) {
-  using C = Cfg<BIG>;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int P = ss.nchunks;
-  const bool small_p = P <= C::kCoffCap;
-  uint32_t* coff = small_p ? sm.coff : p.chunk_off + ss.slot0;
-  if (tid < 32) {  // prefix of the per-chunk candidate counts
-    uint32_t carry = 0;
-    for (int base = 0; base < P; base += 32) {
-      const int c = base + lane;
-      uint32_t n = 0;
-      if (c < P) {
-        n = __ldcg(&p.chunk_count[ss.slot0 + c]);
-        n = n < static_cast<uint32_t>(p.cap) ? n : static_cast<uint32_t>(p.cap);
-      }
-      uint32_t incl = n;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      if (c < P) coff[c] = carry + incl - n;
-      carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
-    }
-    if (lane == 0) {
-      coff[P] = carry;
-      sm.bcast[2] = carry;
-    }
-  }
-  if (!small_p) __threadfence_block();
-  csync();
-  const uint32_t n = sm.bcast[2];
-  const long long len = ss.a1 - ss.a0;
-  if (small_p && n > static_cast<uint32_t>(C::kCacheCap)) {
-    // Too many candidates for the cache: keep only those with key <= kf (the segment's final
-    // threshold), in index order.  Pass 1 counts them per chunk, pass 2 compacts them, one
-    // warp per chunk with ballot ranks.  Usually they fit, and the cache merge runs.
-    const int warp = tid >> 5;
-    for (int c = warp; c < P; c += kWarps) {
-      const uint32_t cnt = sm.coff[c + 1] - sm.coff[c];
-      const uint32_t* src = p.cand + (ss.slot0 + c) * p.cap;
-      uint32_t keep = 0;
-      for (uint32_t i = lane; i < cnt; i += 32) keep += desc_key(__ldcg(src + i) >> 16) <= kf ? 1u : 0u;
-      keep = __reduce_add_sync(0xFFFFFFFFu, keep);
-      if (lane == 0) sm.coff2[c] = keep;
-    }
-    csync();
-    if (tid < 32) {
-      uint32_t carry = 0;
-      for (int base = 0; base < P; base += 32) {
-        const int c = base + lane;
-        const uint32_t v = c < P ? sm.coff2[c] : 0u;
-        uint32_t incl = v;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-          if (lane >= o) incl += y;
-        }
-        if (c < P) sm.coff2[c] = carry + incl - v;
-        carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
-      }
-      if (lane == 0) sm.bcast[2] = carry;
-    }
-    csync();
-    const uint32_t nkeep = sm.bcast[2];
-    if (nkeep <= static_cast<uint32_t>(C::kCacheCap)) {
-      for (int c = warp; c < P; c += kWarps) {
-        const uint32_t cnt = sm.coff[c + 1] - sm.coff[c];
-        const uint32_t* src = p.cand + (ss.slot0 + c) * p.cap;
-        const long long e0 = (ss.v0 + static_cast<long long>(c) * ss.chunk_vecs) * 8;
-        uint32_t dst = sm.coff2[c];
-        for (uint32_t i0 = 0; i0 < cnt; i0 += 32) {
-          const uint32_t i = i0 + lane;
-          uint32_t w = 0;
-          bool keep = false;
-          if (i < cnt) {
-            w = __ldcg(src + i);
-            keep = desc_key(w >> 16) <= kf;
-          }
-          const unsigned b = __ballot_sync(0xFFFFFFFFu, keep);
-          if (keep) sm.cache[dst + __popc(b & ((1u << lane) - 1u))] = make_composite(w, e0, ss.a0);
-          dst += __popc(b);
-        }
-      }
-      csync();
-      emit_from_cache<BIG>(p, sm, nkeep, kf, ss.s, len);
-      return;
-    }
-    // still too many: the merge reads the chunk lists in place (below)
-  }
-  if (small_p && n <= static_cast<uint32_t>(C::kCacheCap)) {
-    const int warp = tid >> 5;
-    for (int c = warp; c < P; c += kWarps) {
-      const uint32_t o = sm.coff[c];
-      const uint32_t cnt = sm.coff[c + 1] - o;
-      const uint32_t* src = p.cand + (ss.slot0 + c) * p.cap;
-      const long long e0 = (ss.v0 + static_cast<long long>(c) * ss.chunk_vecs) * 8;
-      for (uint32_t i = lane; i < cnt; i += 32) {
-        sm.cache[o + i] = make_composite(__ldcg(src + i), e0, ss.a0);
-      }
-    }
-    csync();
-    emit_from_cache<BIG>(p, sm, n, kf, ss.s, len);
-  } else {
-    GlobalSrc gs{&p, coff, P, ss.slot0, ss.v0, ss.a0, ss.chunk_vecs};
-    select_and_emit<BIG>(p, gs, n, kf, ss.s, len, sm);
-  }
-}
-
-// The CTA has finished its chunks of segment ss.s: merge it here if no other CTA still
-// holds some of them.
-template <bool BIG>
-__device__ void close_segment(const TopkParams& p, const SegState& ss, Scratch<BIG>& sm) {
-  if (ss.mycnt == 0) return;
-  uint32_t kf = ss.K;
-  const bool split = ss.mycnt != ss.nchunks;
-  if (split) {
-    __threadfence();  // this thread's candidate writes, before the arrival below
-    csync();
-    if (threadIdx.x == 0) {
-      if (ss.K < kNoThreshold) atomicMin(&p.seg_thresh[ss.s], ss.K);
-      __threadfence();
-      const uint32_t old = atomicAdd(&p.seg_done[ss.s], static_cast<uint32_t>(ss.mycnt));
-      const bool last = old + static_cast<uint32_t>(ss.mycnt) == static_cast<uint32_t>(ss.nchunks);
-      uint32_t k2 = ss.K;
-      if (last) {
-        __threadfence();
-        const uint32_t g = __ldcg(&p.seg_thresh[ss.s]);
-        k2 = g < k2 ? g : k2;
-      }
-      sm.bcast[0] = last ? 1u : 0u;
-      sm.bcast[1] = k2;
-    }
-    csync();
-    if (!sm.bcast[0]) return;
-    kf = sm.bcast[1];
-    __threadfence();
-  }
-  csync();  // every consumer's candidate writes for this segment are done
-  if (!split && !ss.spilled) {
-    emit_from_cache<BIG>(p, sm, ss.nbuf, kf, ss.s, ss.a1 - ss.a0);
-    return;
-  }
-  merge_from_global<BIG>(p, ss, kf, sm);
-}
-
-template <bool BIG>
-__device__ void consumer_loop(const TopkParams& p, uint8_t* stages, uint64_t* full,
-                              uint64_t* empty, const StageInfo* info, Scratch<BIG>& sm) {
-  constexpr int S = Cfg<BIG>::kStagesN;
-  SegState ss;
-  int st = 0, par = 0;
-  uint32_t ph = 0;
-  for (;;) {
-    const bool ok = mbar_wait(&full[st], ph);
-    if (!ok) sm.fail = 1u;
-    const StageInfo& si = info[st];  // read in place: valid until this stage is released
-    const uint8_t* buf = stages + static_cast<size_t>(st) * kStageBytes;
-    int r = kChunkDone;
-    if (si.part == ss.part && ss.strict && si.nvc > 0) {  // uniform: stage info is shared
-      // steady state: one barrier per chunk, usually nothing to write.  After an overflow
-      // (values rising along the row) the next chunk starts from its own threshold instead
-      // of counting everything under the stale one first.
-      if (ss.rising) {
-        bool adopted;
-        r = first_chunk<BIG>(p, si, buf, sm, ss, par, &adopted);
-        ss.rising = adopted;  // still rising while the chunk's own threshold beats the old one
-      } else {
-        r = stream_chunk<true, BIG>(p, si, buf, sm, ss, par);
-        if (r == kChunkOverflow) {
-          r = first_chunk<BIG>(p, si, buf, sm, ss, par);  // values ramped up
-          ss.rising = true;
-        }
-      }
-    } else {
-      if (group_or<kThreads>(!ok)) r = kChunkFail;
-      if (r != kChunkFail) {
-        if (si.part != ss.part) {
-          close_segment<BIG>(p, ss, sm);
-          if (si.part == kStopPart) break;
-          ss = SegState{};
-          ss.s = si.s;
-          ss.part = si.part;
-          ss.nchunks = si.nchunks;
-          ss.chunk_vecs = si.chunk_vecs;
-          ss.slot0 = si.slot - si.c;  // the segment's chunk 0 (the global merge walks all)
-          ss.v0 = si.v0;
-          ss.a0 = si.a0;
-          ss.a1 = si.a1;
-        }
-        if (si.nvc > 0) r = first_chunk<BIG>(p, si, buf, sm, ss, par);
-      }
-    }
-    if (r == kChunkFail) {  // a bulk copy never arrived: stop (the stage contents are not valid)
-      if (threadIdx.x == 0) atomicOr(&p.status[0], kStatusWaitTimeout);
-      return;
-    }
-    if (si.nvc > 0) {
-      ++ss.mycnt;
-      par ^= 1;
-    }
-    release_stage(&empty[st]);
-    if (++st == S) {
-      st = 0;
-      ph ^= 1u;
-    }
-  }
-}
-
-
 #include "bt_small.cuh"
+#include "bt_large.cuh"
 
 
 // 96 registers: each SM sub-partition (16K registers) holds 5 warps, so two 9-warp blocks fit.
@@ -1031,14 +723,14 @@ topk_kernel(TopkParams p) {
   grid_dep_launch();
   if (tid >= kThreads) {
     if (tid == kThreads) {
-      producer_loop<BIG>(p, stages, full, empty, info);
+      producer_loop<BIG>(p, stages, full, empty, info, &sm.fail);
     } else if (!BIG && tid >= kThreads + 32) {
       if constexpr (!BIG) merger_loop(p, sm);
     }
     return;
   }
   if constexpr (BIG) {
-    consumer_loop<true>(p, stages, full, empty, info, sm);
+    consumer_loop_large(p, stages, full, empty, info, sm);
   } else {
     consumer_loop_small(p, stages, full, empty, info, sm);
   }

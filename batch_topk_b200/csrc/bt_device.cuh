@@ -118,6 +118,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// Bounded wait with a caller-given number of tries (0: fail at once without looking).
+__device__ __forceinline__ bool mbar_wait_n(uint64_t* bar, uint32_t parity, uint32_t tries) {
+  for (uint32_t it = 0; it < tries; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  return false;
+}
+
+// Bounded wait that also gives up as soon as *abort becomes non-zero (set by the warps that
+// would complete the phase once they have failed and stopped).
+__device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity,
+                                                const volatile uint32_t* abort) {
+  for (uint32_t it = 0; it < kWaitCap; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+  }
+  return false;
+}
+
 // One bulk global->shared copy (16-byte aligned addresses, size a multiple of 16), completing
 // transaction bytes on `bar`.  No multicast.  Evict-first L2 hint: the input is read once.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,

@@ -74,6 +74,9 @@ struct TopkParams {
   uint16_t* out_values;          // [seg_num * k]
   int* out_indices;              // [seg_num * k]
   uint32_t pad_bits;             // -inf of the element type: the value of a missing entry
+  uint32_t handoff_tries;        // tries of each consumer <-> merger hand-off wait (kWaitCap;
+                                 // fewer only through the failure-path test hook)
+  long long max_total_len;       // CSR: the caller's bound on offsets[seg_num] - offsets[0]
 };
 
 struct SegGeom {
@@ -110,8 +113,7 @@ struct Cfg {
   static constexpr int kStagesN = BIG ? 2 : 3;
   static constexpr int kSelCap = BIG ? kMaxK : 128;      // >= k
   static constexpr int kCacheCap = BIG ? 2048 : 1024;    // merge cache, 64-bit composites
-  static constexpr int kCoffCap = 128;                   // chunks per segment in smem
-  static constexpr int kGroupWords = BIG ? 4 : 1;        // packed group-max key words/thread
+  static constexpr int kGroupWords = 1;                  // packed group-max key words/thread
 };
 
 struct StageInfo {
@@ -138,9 +140,6 @@ struct alignas(16) Scratch {
   uint32_t hist2[256];
   unsigned long long cache[Cfg<BIG>::kCacheCap];
   unsigned long long sel[Cfg<BIG>::kSelCap];
-  alignas(16) uint32_t gkeys[Cfg<BIG>::kGroupWords * kThreads];  // 128-bit reads
-  uint32_t coff[Cfg<BIG>::kCoffCap + 1];
-  uint32_t coff2[Cfg<BIG>::kCoffCap + 1];  // per-chunk offsets of the survivors of the merge filter
   unsigned long long tmask[kThreads];      // balanced write: each thread's candidate bits
   uint32_t tbase[kThreads];                // balanced write: each thread's first output slot
   uint32_t warp_tot[kWarps];
@@ -193,7 +192,7 @@ static_assert(offsetof(Scratch<false>, hist1) % 16 == 0 && offsetof(Scratch<fals
               offsetof(Scratch<false>, gkeys) % 16 == 0 && offsetof(Scratch<false>, wcnt) % 16 == 0,
               "16-byte alignment of lds128 operands");
 static_assert(offsetof(Scratch<true>, hist1) % 16 == 0 && offsetof(Scratch<true>, hist2) % 16 == 0 &&
-              offsetof(Scratch<true>, gkeys) % 16 == 0, "16-byte alignment of lds128 operands");
+              offsetof(Scratch<true>, wcnt) % 16 == 0, "16-byte alignment of lds128 operands");
 
 // Dynamic shared memory: [stages | Scratch | full[] | empty[] | StageInfo[]].
 template <bool BIG>
@@ -250,9 +249,11 @@ __device__ __forceinline__ void decode_part(const TopkParams& p, long long part,
   *c1 = static_cast<int>(static_cast<long long>(j + 1) * n / pps);
 }
 
+// `abort` is the block's failure flag: once the consumers have failed and stopped releasing
+// stages, a wait for a free stage gives up at once instead of running out its tries.
 template <bool BIG>
 __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* full,
-                              uint64_t* empty, StageInfo* info) {
+                              uint64_t* empty, StageInfo* info, const uint32_t* abort) {
   constexpr int S = Cfg<BIG>::kStagesN;
   const uint64_t policy = policy_evict_first();
   const long long nparts = total_parts(p);
@@ -262,7 +263,8 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
   bool ok = true;
   // one stage: wait for it to be free, fill its info, start the copy (or just signal)
   auto put = [&](const StageInfo& si) -> bool {
-    if (round > 0 && !mbar_wait(&empty[st], static_cast<uint32_t>((round - 1) & 1))) {
+    if (round > 0 && !mbar_wait_abort(&empty[st], static_cast<uint32_t>((round - 1) & 1),
+                                      abort)) {
       atomicOr(&p.status[0], kStatusWaitTimeout);
       return false;
     }
@@ -560,8 +562,10 @@ __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
   }
   if (tid == 0) {
     p.chunk_start[p.seg_num] = carry;
-    // chunks beyond the workspace capacity: process no part at all and flag the call
-    const bool over = static_cast<long long>(carry) > p.slot_capacity;
+    // offsets spanning more than max_total_len values, or chunks beyond the workspace
+    // capacity: process no part at all and flag the call
+    const long long span = static_cast<long long>(p.offsets[p.seg_num]) - p.offsets[0];
+    const bool over = static_cast<long long>(carry) > p.slot_capacity || span > p.max_total_len;
     p.part_start[p.seg_num] = over ? 0u : pcarry;
     if (over) atomicOr(&p.status[0], kStatusBadOffsets);
   }

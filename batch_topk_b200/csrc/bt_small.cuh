@@ -95,9 +95,11 @@ __device__ __forceinline__ void write_batch(const StageInfo& si, const uint8_t* 
 }
 
 // Waits until batch buffer b may be overwritten (the merger released its previous use).
-__device__ __forceinline__ bool wait_batch_free(SmallScratch& sm, long long nb) {
+__device__ __forceinline__ bool wait_batch_free(const TopkParams& p, SmallScratch& sm,
+                                                long long nb) {
   if (nb < 2) return true;
-  return mbar_wait(&sm.batch_free[nb & 1], static_cast<uint32_t>(((nb >> 1) - 1) & 1));
+  return mbar_wait_n(&sm.batch_free[nb & 1], static_cast<uint32_t>(((nb >> 1) - 1) & 1),
+                     p.handoff_tries);
 }
 
 __device__ __forceinline__ void send_batch(SmallScratch& sm, int b, const BatchMeta& meta) {
@@ -175,7 +177,7 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
       uint64_t S;
       uint32_t sbase, stot;
       const uint32_t kstar = exact_local_select(p, si, buf, sm, K, strict, &S, &sbase, &stot);
-      if (!wait_batch_free(sm, nb)) sm.fail = 1u;  // caught at the next barrier
+      if (!wait_batch_free(p, sm, nb)) sm.fail = 1u;  // caught at the next barrier
       const int tid = threadIdx.x;
       const long long e0 = si.cv0 * 8;
       uint32_t r = 0;
@@ -191,7 +193,7 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
   }
   const bool send = n > 0 || si.last;  // empty middle chunks need no hand-off
   if (!written && send) {
-    if (!wait_batch_free(sm, nb)) sm.fail = 1u;  // caught at the next barrier
+    if (!wait_batch_free(p, sm, nb)) sm.fail = 1u;  // caught at the next barrier
     if (c.flags) {
       if (strict) write_batch<true>(si, buf, c.flags, K, c.base, sm.batch[b]);
       else write_batch<false>(si, buf, c.flags, K, c.base, sm.batch[b]);
@@ -276,7 +278,7 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
         done = !group_or<kThreads>(f != 0 || sm.fail != 0);
         if (done) ss.quiet = true;
         if (done && last) {  // nothing passed in the part's last chunk: the end marker
-          if (!wait_batch_free(sm, nb)) sm.fail = 1u;  // seen by all at the next barrier
+          if (!wait_batch_free(p, sm, nb)) sm.fail = 1u;  // seen by all at the next barrier
           BatchMeta meta;
           meta.len = si.a1 - si.a0;
           meta.part_slot = ss.slot0;
@@ -310,7 +312,7 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
     }
   }
   // tell the merger to stop (bounded wait for the buffer)
-  wait_batch_free(sm, nb);
+  wait_batch_free(p, sm, nb);
   csync();
   if ((failed || sm.fail) && threadIdx.x == 0) atomicOr(&p.status[0], kStatusWaitTimeout);
   BatchMeta stop{};
@@ -537,7 +539,7 @@ __device__ void merger_loop_r(const TopkParams& p, SmallScratch& sm) {
   int nl = 0;
   for (;;) {
     const int b = static_cast<int>(nbm & 1);
-    if (!mbar_wait(&sm.batch_full[b], static_cast<uint32_t>((nbm >> 1) & 1))) {
+    if (!mbar_wait_n(&sm.batch_full[b], static_cast<uint32_t>((nbm >> 1) & 1), p.handoff_tries)) {
       if (lane == 0) atomicOr(&p.status[0], kStatusWaitTimeout);
       return;
     }

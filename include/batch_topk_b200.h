@@ -111,11 +111,26 @@ int bt_topk_half_noalloc(const void* d_input, int seg_num, int seg_len, int k,
  * previous segment's (verified), and one reserved word. */
 #define BT_STATS_WORDS 6
 #define BT_STATUS_OK 0
-#define BT_STATUS_WAIT_TIMEOUT 1    /* a bulk-copy wait hit its iteration cap */
+#define BT_STATUS_WAIT_TIMEOUT 1    /* a bounded wait (bulk copy, hand-off) hit its cap */
 #define BT_STATUS_BAD_OFFSETS 2     /* CSR offsets decreasing or beyond max_total_len */
 #define BT_STATUS_SEGMENT_TOO_LONG 4
 #define BT_STATUS_CERTIFY_FAILED 8  /* fewer candidates than the threshold certified */
 int bt_workspace_status(const void* d_workspace, int seg_num, void* stream, unsigned* stats);
+
+/* bt_workspace_status for the no-allocation entry point: reads back (synchronously, on
+ * `stream`) the status word and counters of the last bt_topk_half_noalloc call on the current
+ * device, from the library's fixed scratch array.  No reference counterpart (the reference
+ * reports device-side problems only through cudaGetLastError, src/batch_topk.cu:85-193).
+ * Allocates nothing.  Returns the BT_STATUS_* flags, or a negated cudaError_t code. */
+int bt_noalloc_status(void* stream, unsigned* stats);
+
+/* Failure-path test hook (no reference counterpart): the number of tries each consumer <->
+ * merger hand-off wait of the k <= 128 kernel makes before it gives up, for calls launched
+ * after this one, process-wide.  0 makes those waits fail at once, so a call ends early with
+ * BT_STATUS_WAIT_TIMEOUT set and its outputs undefined; a negative value restores the default
+ * (about a second of waiting).  The waits for bulk copies already in flight are never
+ * shortened.  Not for concurrent callers. */
+void bt_set_handoff_wait_tries(int tries);
 
 /* Optional timing hook: when both are non-NULL cudaEvent_t handles, every later call records
  * ev_start just before its main (streaming) kernel and ev_stop just after it, on the call's

@@ -17,6 +17,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 REF_LIB_PATH = os.path.join(HERE, "_ref", "libref_oracle.so")
+REF_GPU_LIB_PATH = os.path.join(HERE, "_ref", "libref_gpu.so")
 _lock = threading.Lock()
 _oracle = None
 _ref = None
@@ -25,10 +26,25 @@ METHOD_SORT = 0  # the reference's algorithm: sort the index permutation
 METHOD_COUNT = 1  # counting select on the descending key, same order, O(n)
 
 
+def reference_dir() -> str | None:
+    """The reference tree (fire-emblem/batch_topk) if it is present: the directory named by
+    BT_REFERENCE_DIR, else a ``reference`` directory beside this repository; None otherwise."""
+    cands = [os.environ.get("BT_REFERENCE_DIR"),
+             os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")]
+    for d in cands:
+        if d and os.path.isfile(os.path.join(d, "include", "batch_topk_types.cuh")):
+            return d
+    return None
+
+
 def build(ref: bool = True) -> None:
     """Compile the checker (and, when the reference tree exists, oracle/_ref)."""
     targets = ["all"] if ref else ["oracle"]
-    subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
+    cmd = ["make", "-s", "-C", HERE, *targets]
+    rd = reference_dir() if ref else None
+    if rd:
+        cmd.append(f"REF={rd}")
+    subprocess.run(cmd, check=True)
 
 
 def encode_desc(bits: np.ndarray) -> np.ndarray:
@@ -194,6 +210,35 @@ def load() -> Oracle:
                 build(ref=False)
             _oracle = Oracle()
         return _oracle
+
+
+class RefGpu:
+    """The reference's own GPU path (its src/batch_topk.cu for sm_100a), built into
+    oracle/_ref/libref_gpu.so: radix_topk::batch_topk_half behind a C ABI, for timing it next
+    to this library on the reference's own supported shapes."""
+
+    def __init__(self, path: str = REF_GPU_LIB_PATH):
+        lib = C.CDLL(path)
+        vp, i32 = C.c_void_p, C.c_int
+        lib.ref_gpu_topk_half.argtypes = [vp, i32, i32, i32, vp, vp, vp, C.c_size_t, vp]
+        lib.ref_gpu_topk_half.restype = i32
+        lib.ref_gpu_workspace_size.argtypes = [i32, i32, i32]
+        lib.ref_gpu_workspace_size.restype = C.c_size_t
+        self.lib = lib
+
+    def workspace_size(self, seg_num: int, seg_len: int, k: int) -> int:
+        return int(self.lib.ref_gpu_workspace_size(seg_num, seg_len, k))
+
+    def topk_half(self, d_in, seg_num, seg_len, k, d_vals, d_idx, d_ws, ws_bytes, stream=0) -> int:
+        return int(self.lib.ref_gpu_topk_half(d_in, seg_num, seg_len, k, d_vals, d_idx, d_ws,
+                                              ws_bytes, stream))
+
+
+def load_ref_gpu() -> RefGpu | None:
+    """Load the reference's GPU path if it was built here (None otherwise)."""
+    if not os.path.exists(REF_GPU_LIB_PATH):
+        return None
+    return RefGpu()
 
 
 def load_ref() -> RefOracle | None:

@@ -33,10 +33,18 @@ def test_host_caller_builds_and_passes(tmp_path):
     assert "FAIL" not in res.stdout and res.stdout.count("ok ") >= 14
 
 
-REF_BENCH = os.path.join(os.sep, "root", "reference", "bench", "bench_batch_topk.cu")
+def _ref_bench():
+    import oracle
+
+    d = oracle.reference_dir()  # BT_REFERENCE_DIR, or a reference tree beside the repository
+    return os.path.join(d, "bench", "bench_batch_topk.cu") if d else ""
 
 
-@pytest.mark.skipif(not os.path.exists(REF_BENCH), reason="reference tree not present")
+REF_BENCH = _ref_bench()
+
+
+@pytest.mark.skipif(not REF_BENCH or not os.path.exists(REF_BENCH),
+                    reason="reference tree not present (set BT_REFERENCE_DIR)")
 def test_reference_benchmark_driver_builds_against_headers(tmp_path):
     exe = tmp_path / "bench_dropin"
     nvcc = "/usr/local/cuda/bin/nvcc"

@@ -99,3 +99,50 @@ def test_segmented_operator(orc):
     exp_v, exp_i = orc.topk_csr(vals, off, 50)
     assert_exact(v.cpu().view(torch.int16).numpy().view(np.uint16), i.cpu().numpy(), exp_v, exp_i,
                  "segmented op vs oracle")
+
+
+@pytest.mark.gpu
+def test_two_explicit_streams_get_separate_workspaces(orc):
+    """Calls on two explicit streams under one current stream each use the default workspace
+    of their own launch stream, so overlapping calls do not race on a shared buffer."""
+    import torch
+
+    from batch_topk_b200.torch_api import topk
+
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(31)
+    a = rng.standard_normal((256, 151936)).astype(np.float16)
+    b = rng.standard_normal((256, 151936)).astype(np.float16)
+    xa = torch.from_numpy(a).to(dev)
+    xb = torch.from_numpy(b).to(dev)
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s1.wait_stream(torch.cuda.current_stream(dev))
+    s2.wait_stream(torch.cuda.current_stream(dev))
+    outs = []
+    for _ in range(3):
+        outs.append(topk(xa, 50, stream=s1) + (a,))
+        outs.append(topk(xb, 50, stream=s2) + (b,))
+    torch.cuda.synchronize(dev)
+    for v, i, src in outs:
+        exp_v, exp_i = orc.topk(src.view(np.uint16), 50)
+        assert np.array_equal(i.cpu().numpy(), exp_i)
+        assert np.array_equal(v.cpu().numpy().view(np.uint16), exp_v)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_input_on_another_device_than_the_current_one(orc):
+    """x on cuda:1 while cuda:0 is current: the call runs on x's device."""
+    from batch_topk_b200.torch_api import topk
+
+    rng = np.random.default_rng(32)
+    a = rng.standard_normal((64, 40000)).astype(np.float16)
+    with torch.cuda.device(0):
+        x = torch.from_numpy(a).to("cuda:1")
+        v, i = topk(x, 50)
+        assert v.device == x.device and i.device == x.device
+        torch.cuda.synchronize(1)
+    exp_v, exp_i = orc.topk(a.view(np.uint16), 50)
+    assert np.array_equal(i.cpu().numpy(), exp_i)
+    assert np.array_equal(v.cpu().numpy().view(np.uint16), exp_v)

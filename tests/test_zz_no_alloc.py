@@ -117,3 +117,30 @@ def test_noalloc_rejects_oversized_and_invalid_shapes():
     for shape in ((0, 100, 1), (4, 100, 0), (4, 100, 101), (4, 5000, bt.MAX_K + 1)):
         assert bt.batch_topk_half_noalloc(fake, *shape, fake, fake, 0) == \
             bt.CUDA_ERROR_INVALID_VALUE
+
+
+@pytest.mark.gpu
+def test_noalloc_status_readback():
+    """bt_noalloc_status reads the status word of the last no-alloc call from the fixed
+    scratch array, so a failed device-side check is visible to callers of the no-alloc entry
+    point too: clean after an ordinary call, BT_STATUS_WAIT_TIMEOUT after a call whose
+    hand-off waits were made to give up at once, and clean (and exact) again after that."""
+    import torch
+
+    dev = torch.device("cuda:0")
+    s = torch.cuda.current_stream(dev)
+    seg_num, seg_len, k = 8, 151936, 50
+    bits = _gen(seg_num, seg_len, seed=77)
+    _buf, x = _dev_copy(torch, bits, 0, dev)
+    ref_v, ref_i = _run(torch, x, seg_num, seg_len, k, noalloc=False, stream=s)
+    _run(torch, x, seg_num, seg_len, k, noalloc=True, stream=s)
+    assert bt.noalloc_status(s.cuda_stream)[0] == 0
+    bt.set_handoff_wait_tries(0)
+    try:
+        _run(torch, x, seg_num, seg_len, k, noalloc=True, stream=s)
+    finally:
+        bt.set_handoff_wait_tries(None)
+    assert bt.noalloc_status(s.cuda_stream)[0] & bt.STATUS_WAIT_TIMEOUT
+    v, i = _run(torch, x, seg_num, seg_len, k, noalloc=True, stream=s)
+    assert bt.noalloc_status(s.cuda_stream)[0] == 0
+    assert np.array_equal(i, ref_i) and np.array_equal(v, ref_v)
