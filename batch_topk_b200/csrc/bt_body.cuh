@@ -152,8 +152,8 @@ __device__ __forceinline__ bool pass_any(const uint4& w, h2t v2) {
 
 // This thread's 8 vectors (tid*8 .. tid*8+7): exact candidate mask of vector j, with the
 // segment-boundary and take-all (no threshold yet) cases.
-// Half e (element order) of a 16-byte vector; e must be a compile-time constant after
-// unrolling, so the word is picked without indexing a register array.
+// Half e (element order) of a 16-byte vector, picked by selects, so neither a compile-time
+// nor a run-time e indexes a register array.
 __device__ __forceinline__ uint32_t vec_half(const uint4& w, int e) {
   const uint32_t word = e < 2 ? w.x : (e < 4 ? w.y : (e < 6 ? w.z : w.w));
   return (e & 1) ? (word >> 16) : (word & 0xFFFFu);
@@ -237,76 +237,29 @@ __device__ __forceinline__ unsigned long long make_composite(uint32_t word, long
          (static_cast<unsigned long long>(idx) << 16) | raw;
 }
 
-// Writes this thread's candidates (flagged vectors, index order) as (key, index, bits)
-// composites at sm.cache[nbuf + base ...].
-template <bool STRICT, bool BIG>
-__device__ __forceinline__ void write_flagged(const StageInfo& si, const uint8_t* buf,
-                                              uint32_t flags, h2t v2, bool take_all,
-                                              uint32_t base, Scratch<BIG>& sm, uint32_t nbuf) {
-  const int tid = threadIdx.x;
-  const long long e0 = si.cv0 * 8;
-  const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf);
-  unsigned long long* out = sm.cache + nbuf + base;
-  uint32_t r = 0;
-  while (flags) {
-    const int j = __ffs(flags) - 1;
-    flags &= flags - 1;
-    const int vi = tid * kVecPerThread + j;
-    uint32_t m = vec_mask<STRICT>(si, buf, vi, v2, take_all);
-    while (m) {
-      const int e = __ffs(m) - 1;
-      m &= m - 1;
-      const uint32_t lidx = static_cast<uint32_t>(vi * 8 + e);
-      out[r++] = make_composite((static_cast<uint32_t>(v16[lidx]) << 16) | lidx, e0, si.a0);
-    }
-  }
-}
-
-// k-th smallest key among the n composites of the segment buffer, searched in [0, hi]
-// (kFewerThanK when fewer than k of them have key <= hi: then every candidate qualifies).  Each warp computes it independently (no barrier).
-template <bool BIG>
-__device__ __forceinline__ uint32_t buffer_kth_key(const Scratch<BIG>& sm, uint32_t n, uint32_t k,
-                                                   uint32_t hi) {
-  if (n < k) return kFewerThanK;
-  const int lane = threadIdx.x & 31;
-  {
-    uint32_t cnt = 0;
-    for (uint32_t i = lane; i < n; i += 32) cnt += static_cast<uint32_t>(sm.cache[i] >> 48) <= hi;
-    if (__reduce_add_sync(0xFFFFFFFFu, cnt) < k) return kFewerThanK;
-  }
-  uint32_t lo = 0;
-  while (lo < hi) {
-    const uint32_t mid = (lo + hi) >> 1;
-    uint32_t cnt = 0;
-    for (uint32_t i = lane; i < n; i += 32) {
-      cnt += static_cast<uint32_t>(sm.cache[i] >> 48) <= mid ? 1u : 0u;
-    }
-    if (__reduce_add_sync(0xFFFFFFFFu, cnt) >= k) hi = mid; else lo = mid + 1;
-  }
-  return lo;
-}
-
 // Block-wide k-th smallest key among the n composites of the segment buffer: two 8-bit digit
-// histograms (aggregated shared atomics) instead of a per-warp search over the whole buffer.
-// kFewerThanK when n < k.  The histograms are zero on entry and left zero.
+// histograms.  Each thread takes a contiguous run of entries (the buffer is in index order, so
+// tie-heavy and sorted data give long runs of one bin) and adds run lengths with plain shared
+// atomics.  kFewerThanK when n < k.  The histograms are zero on entry and left zero.
 template <bool BIG>
 __device__ uint32_t buffer_kth_key_block(Scratch<BIG>& sm, uint32_t n, uint32_t k) {
   if (n < k) return kFewerThanK;
   const int tid = threadIdx.x;
-  for (uint32_t i0 = 0; i0 < n; i0 += kThreads) {
-    const uint32_t i = i0 + tid;
-    const uint32_t key = i < n ? static_cast<uint32_t>(sm.cache[i] >> 48) : 0u;
-    hist_add_match(sm.hist1, key >> 8, i < n);
-  }
+  const uint32_t R = (n + kThreads - 1) / kThreads;
+  const uint32_t i0 = tid * R < n ? tid * R : n;
+  const uint32_t i1 = i0 + R < n ? i0 + R : n;
+  RunHist rh;
+  for (uint32_t i = i0; i < i1; ++i) rh.add(sm.hist1, static_cast<uint32_t>(sm.cache[i] >> 56));
+  rh.flush(sm.hist1);
   csync();
   if (tid < 32) warp_find_bin(sm.hist1, 0, k, &sm.bin1, &sm.before1);
   csync();
   const uint32_t b1 = static_cast<uint32_t>(sm.bin1);
-  for (uint32_t i0 = 0; i0 < n; i0 += kThreads) {
-    const uint32_t i = i0 + tid;
-    const uint32_t key = i < n ? static_cast<uint32_t>(sm.cache[i] >> 48) : 0u;
-    hist_add_match(sm.hist2, key & 0xFFu, i < n && (key >> 8) == b1);
+  for (uint32_t i = i0; i < i1; ++i) {
+    const uint32_t key = static_cast<uint32_t>(sm.cache[i] >> 48);
+    if ((key >> 8) == b1) rh.add(sm.hist2, key & 0xFFu);
   }
+  rh.flush(sm.hist2);
   csync();
   if (tid < 32) warp_find_bin(sm.hist2, sm.before1, k, &sm.bin2, &sm.before2);
   csync();
@@ -447,238 +400,12 @@ __device__ uint32_t compact_cache(Scratch<BIG>& sm, uint32_t n, uint32_t K, uint
   return (tot & 0xFFFFu) + (ties < need ? ties : need);
 }
 
-// Position of the r-th set bit (r from 0) of a 64-bit mask.
-__device__ __forceinline__ int select_bit64(unsigned long long m, uint32_t r) {
-  const uint32_t lo = static_cast<uint32_t>(m);
-  const uint32_t pl = static_cast<uint32_t>(__popc(lo));
-  uint32_t w = r < pl ? lo : static_cast<uint32_t>(m >> 32);
-  uint32_t rr = r < pl ? r : r - pl;
-  int pos = r < pl ? 0 : 32;
-#pragma unroll
-  for (int width = 16; width >= 1; width >>= 1) {
-    const uint32_t c = static_cast<uint32_t>(__popc(w & ((1u << width) - 1u)));
-    if (rr >= c) {
-      rr -= c;
-      w >>= width;
-      pos += width;
-    }
-  }
-  return pos;
-}
-
-// Writes the chunk's `total` candidates in index order like write_flagged, but spread over the
-// block: every thread takes output slots tid, tid + kThreads, ... and finds each one's owner
-// thread (binary search over the prefixes) and element (the rank-th set bit of the owner's
-// mask).  For clustered candidates (a sorted row's top values sit in a few threads) this keeps
-// the block from waiting on a few serial writers.
-template <bool STRICT, bool BIG>
-__device__ void write_balanced(const StageInfo& si, const uint8_t* buf, uint32_t flags, h2t v2,
-                               bool take_all, uint32_t base, uint32_t total, Scratch<BIG>& sm,
-                               uint32_t nbuf) {
-  const int tid = threadIdx.x;
-  unsigned long long M = 0;
-  for (uint32_t f = flags; f; f &= f - 1) {
-    const int j = __ffs(f) - 1;
-    M |= static_cast<unsigned long long>(vec_mask<STRICT>(si, buf, tid * kVecPerThread + j, v2,
-                                                          take_all)) << (8 * j);
-  }
-  sm.tmask[tid] = M;
-  sm.tbase[tid] = base;
-  csync();
-  const uint16_t* v16 = reinterpret_cast<const uint16_t*>(buf);
-  const long long e0 = si.cv0 * 8;
-  for (uint32_t i = tid; i < total; i += kThreads) {
-    int lo = 0, hi = kThreads - 1;  // owner: the last thread whose first slot is <= i
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (sm.tbase[mid] <= i) lo = mid; else hi = mid - 1;
-    }
-    const int pos = select_bit64(sm.tmask[lo], i - sm.tbase[lo]);
-    const uint32_t lidx = static_cast<uint32_t>(lo * 64 + pos);
-    sm.cache[nbuf + i] = make_composite((static_cast<uint32_t>(v16[lidx]) << 16) | lidx, e0, si.a0);
-  }
-  csync();  // tmask / tbase are free again
-}
-
-// ---- consumer: segment merge -----------------------------------------------------------
-
-// Candidate source for the merge: the shared-memory cache or the chunk lists in global
-// memory (very long segments, many candidates, or a segment split across blocks).
-struct CacheSrc {
-  const unsigned long long* cache;
-  __device__ __forceinline__ unsigned long long get(uint32_t i) const { return cache[i]; }
-};
-
-// Each of the n candidates with key <= kf takes the output slot given by its rank in
-// (key, index) order among them; composites are distinct, so ranks are exact.  Every
-// candidate ranking below another one with key <= kf also has key <= kf.
-__device__ __forceinline__ void rank_emit(const TopkParams& p, const unsigned long long* items,
-                                          uint32_t n, uint32_t kf, int s, long long len) {
-  const int tid = threadIdx.x;
-  const uint32_t k = static_cast<uint32_t>(p.k);
-  uint16_t* ov = p.out_values + static_cast<long long>(s) * k;
-  int* oi = p.out_indices + static_cast<long long>(s) * k;
-  for (uint32_t e = tid; e < n; e += kThreads) {
-    const unsigned long long c = items[e];
-    if (static_cast<uint32_t>(c >> 48) > kf) continue;
-    uint32_t rank = 0;
-    for (uint32_t j = 0; j < n; ++j) rank += items[j] < c ? 1u : 0u;
-    if (rank < k) {
-      ov[rank] = static_cast<uint16_t>(c & 0xFFFFu);
-      oi[rank] = static_cast<int>((c >> 16) & 0xFFFFFFFFu);
-    }
-  }
-  // A segment shorter than k never certifies a threshold, so all n candidates are its
-  // values; the rest of the row is padding.
-  if (len < static_cast<long long>(k)) {
-    for (uint32_t r = n + tid; r < k; r += kThreads) {
-      ov[r] = kNegInfBits;
-      oi[r] = -1;
-    }
-  }
-  if (tid == 0 && p.stats) atomicAdd(&p.status[4], 1u);
-}
-
-// Exact top-k of the n candidates of `src` (index order) with key <= kf; writes row s.
-template <bool BIG, class Src>
-__device__ void select_and_emit(const TopkParams& p, const Src& src, uint32_t n, uint32_t kf,
-                                int s, long long seg_len, Scratch<BIG>& sm) {
-  const int tid = threadIdx.x;
-  const uint32_t k = static_cast<uint32_t>(p.k);
-  const uint32_t R = (n + kThreads - 1) / kThreads;
-  const uint32_t i0 = tid * R < n ? tid * R : n;
-  const uint32_t i1 = i0 + R < n ? i0 + R : n;
-  for (uint32_t j = 0; j < R; ++j) {
-    const uint32_t i = i0 + j;
-    uint32_t key = 0xFFFFFFFFu;
-    if (i < i1) key = static_cast<uint32_t>(src.get(i) >> 48);
-    hist_add_match(sm.hist1, key >> 8, key <= kf);
-  }
-  csync();
-  if (tid < 32) warp_find_bin(sm.hist1, 0, k, &sm.bin1, &sm.before1);
-  csync();
-  const int b1 = sm.bin1;
-  uint32_t kstar, need;
-  if (b1 >= 256) {  // fewer than k candidates (a segment shorter than k): keep them all
-    kstar = 0x10000u;
-    need = 0;
-  } else {
-    for (uint32_t j = 0; j < R; ++j) {
-      const uint32_t i = i0 + j;
-      uint32_t key = 0xFFFFFFFFu;
-      if (i < i1) key = static_cast<uint32_t>(src.get(i) >> 48);
-      hist_add_match(sm.hist2, key & 0xFFu, key <= kf && (key >> 8) == static_cast<uint32_t>(b1));
-    }
-    csync();
-    if (tid < 32) warp_find_bin(sm.hist2, sm.before1, k, &sm.bin2, &sm.before2);
-    csync();
-    kstar = (static_cast<uint32_t>(b1) << 8) | static_cast<uint32_t>(sm.bin2);
-    need = k - sm.before2;
-  }
-  // ordered ranks of the ties at the cutoff
-  uint32_t tcnt = 0;
-  for (uint32_t i = i0; i < i1; ++i) {
-    const uint32_t key = static_cast<uint32_t>(src.get(i) >> 48);
-    tcnt += (key <= kf && key == kstar) ? 1u : 0u;
-  }
-  uint32_t ttot;
-  const uint32_t tbase = block_excl_scan<kThreads, true>(tcnt, &ttot, sm.warp_tot);
-  uint32_t scnt = 0;
-  {
-    uint32_t tr = tbase;
-    for (uint32_t i = i0; i < i1; ++i) {
-      const uint32_t key = static_cast<uint32_t>(src.get(i) >> 48);
-      if (key > kf) continue;
-      if (key < kstar) {
-        ++scnt;
-      } else if (key == kstar) {
-        scnt += tr < need ? 1u : 0u;
-        ++tr;
-      }
-    }
-  }
-  uint32_t nsel;
-  const uint32_t sbase = block_excl_scan<kThreads, true>(scnt, &nsel, sm.warp_tot);
-  {
-    uint32_t tr = tbase, w = sbase;
-    for (uint32_t i = i0; i < i1; ++i) {
-      const unsigned long long c = src.get(i);
-      const uint32_t key = static_cast<uint32_t>(c >> 48);
-      if (key > kf) continue;
-      bool take = key < kstar;
-      if (key == kstar) {
-        take = tr < need;
-        ++tr;
-      }
-      if (take) sm.sel[w++] = c;
-    }
-  }
-  csync();
-  uint16_t* ov = p.out_values + static_cast<long long>(s) * k;
-  int* oi = p.out_indices + static_cast<long long>(s) * k;
-  if (nsel <= static_cast<uint32_t>(kThreads)) {
-    rank_emit(p, sm.sel, nsel, 0xFFFFu, s, 0);
-  } else {
-    int n2 = 1;
-    while (n2 < static_cast<int>(nsel)) n2 <<= 1;
-    for (int i = static_cast<int>(nsel) + tid; i < n2; i += kThreads) sm.sel[i] = ~0ull;
-    csync();
-    for (int size = 2; size <= n2; size <<= 1) {
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        for (int i = tid; i < n2 / 2; i += kThreads) {
-          const int lo = 2 * i - (i & (stride - 1));
-          const int hi = lo + stride;
-          const bool up = (lo & size) == 0;
-          const unsigned long long a = sm.sel[lo], b = sm.sel[hi];
-          if ((a > b) == up) {
-            sm.sel[lo] = b;
-            sm.sel[hi] = a;
-          }
-        }
-        csync();
-      }
-    }
-    for (uint32_t r = tid; r < nsel; r += kThreads) {
-      const unsigned long long c = sm.sel[r];
-      ov[r] = static_cast<uint16_t>(c & 0xFFFFu);
-      oi[r] = static_cast<int>((c >> 16) & 0xFFFFFFFFu);
-    }
-    if (tid == 0 && p.stats) atomicAdd(&p.status[4], 1u);
-  }
-  for (uint32_t r = nsel + tid; r < k; r += kThreads) {
-    ov[r] = kNegInfBits;
-    oi[r] = -1;
-  }
-  if (tid == 0 && nsel < k && seg_len >= static_cast<long long>(k)) {
-    atomicOr(&p.status[0], kStatusCertifyFailed);
-  }
-  sm.hist1[tid] = 0;
-  sm.hist2[tid] = 0;
-  csync();
-}
-
-// Emits row s from the n candidates in sm.cache (key <= kf qualifies).
-template <bool BIG>
-__device__ __forceinline__ void emit_from_cache(const TopkParams& p, Scratch<BIG>& sm, uint32_t n,
-                                                uint32_t kf, int s, long long len) {
-  const uint32_t k = static_cast<uint32_t>(p.k);
-  if (!BIG) {
-    const uint32_t kk = buffer_kth_key(sm, n, k, kf);  // exact cutoff key of the row
-    if (kk == kFewerThanK && len >= static_cast<long long>(k) && threadIdx.x == 0) {
-      atomicOr(&p.status[0], kStatusCertifyFailed);  // fewer than k candidates survived
-    }
-    rank_emit(p, sm.cache, n, kk, s, len);
-  } else {
-    CacheSrc cs{sm.cache};
-    select_and_emit<BIG>(p, cs, n, kf, s, len, sm);
-  }
-}
-
 #include "bt_small.cuh"
 #include "bt_large.cuh"
 
 
-// 96 registers: each SM sub-partition (16K registers) holds 5 warps, so two 9-warp blocks fit.
+// 96 registers: each SM sub-partition (16K registers) holds 5 warps, so two blocks of 9 or 10
+// warps fit on an SM (with 112, a sub-partition would hold only 4 warps: one block per SM).
 template <bool BIG>
 __global__ void __maxnreg__(96)
 topk_kernel(TopkParams p) {

@@ -139,11 +139,10 @@ struct alignas(16) Scratch {
   uint32_t hist1[256];  // 16-byte aligned: warp_find_bin reads it with 128-bit loads
   uint32_t hist2[256];
   unsigned long long cache[Cfg<BIG>::kCacheCap];
-  unsigned long long sel[Cfg<BIG>::kSelCap];
-  unsigned long long tmask[kThreads];      // balanced write: each thread's candidate bits
-  uint32_t tbase[kThreads];                // balanced write: each thread's first output slot
+  uint32_t tbase[kThreads];                // split-segment merge: list lengths of 256 slots
   uint32_t warp_tot[kWarps];
   alignas(16) uint32_t wcnt[2][kWarps];  // per-warp candidate counts, double-buffered
+  alignas(16) uint32_t rw[2][kWarps][8];  // strided counts: per-warp round totals (16-bit packed)
   int bin1, bin2;
   uint32_t before1, before2;
   uint32_t bcast[4];
@@ -192,7 +191,8 @@ static_assert(offsetof(Scratch<false>, hist1) % 16 == 0 && offsetof(Scratch<fals
               offsetof(Scratch<false>, gkeys) % 16 == 0 && offsetof(Scratch<false>, wcnt) % 16 == 0,
               "16-byte alignment of lds128 operands");
 static_assert(offsetof(Scratch<true>, hist1) % 16 == 0 && offsetof(Scratch<true>, hist2) % 16 == 0 &&
-              offsetof(Scratch<true>, wcnt) % 16 == 0, "16-byte alignment of lds128 operands");
+              offsetof(Scratch<true>, wcnt) % 16 == 0 && offsetof(Scratch<true>, rw) % 16 == 0,
+              "16-byte alignment of lds128 operands");
 
 // Dynamic shared memory: [stages | Scratch | full[] | empty[] | StageInfo[]].
 template <bool BIG>

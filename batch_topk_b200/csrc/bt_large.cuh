@@ -23,7 +23,7 @@ struct LargeState {
   bool quiet = false;         // the previous chunk of the part added nothing
   bool rising = false;        // the previous chunk beat the stale threshold (values ramp up)
   uint32_t nbuf = 0;          // candidates in sm.cache
-  uint32_t added = 0;         // candidates added since K was last tightened from the cache
+  uint32_t added = 0;         // candidates appended since K was last tightened from the cache
   int mycnt = 0;              // chunks of this part processed
   int nchunks = 0;            // chunks of the segment
   long long part_slot = 0;    // slot of the part's first chunk: its partial list lives there
@@ -31,73 +31,217 @@ struct LargeState {
   long long a0 = 0, a1 = 0;   // aligned element coordinates of the segment
 };
 
-struct LCount {
-  uint32_t flags, cnt, base, total;
+// ---- strided count and append --------------------------------------------------------
+//
+// For the count and the append, thread t owns vectors t + kThreads * j of the chunk, j = 0..7
+// ("round j").  Round-major order (round, thread, element) is index order, and survivors
+// clustered in one stretch of the chunk (sorted rows) spread over every thread.  Positions come
+// from per-round warp scans of 16-bit packed counts and one barrier.
+struct SCount {
+  uint64_t M;         // survivors: bit 8 j + e = element e of the thread's round-j vector
+  uint64_t E;         // tie mode: the survivors whose key equals the threshold (subset of M)
+  uint32_t base[4];   // per round (16-bit fields): index-order rank of the thread's first
+                      // survivor among the round-major survivors (tie mode: among key < T)
+  uint32_t ebase[4];  // tie mode, per round: survivors with key == T ahead of the thread's first
+  uint32_t total;     // survivors (tie mode: those with key < T)
+  uint32_t total_eq;  // tie mode: survivors with key == T
   bool fail;
 };
 
-// Counts the chunk's candidates under (K, STRICT) with one barrier: per-thread vector flags and
-// counts, the thread's first output position and the block total.  `par` alternates the
-// per-warp count slots so consecutive counts need no barrier between them.
-template <bool STRICT>
-__device__ __forceinline__ LCount large_count(const StageInfo& si, const uint8_t* buf,
-                                              LargeScratch& sm, uint32_t K, int& par) {
+// 16-bit field j of four packed words (selects rather than indexing, so a run-time j keeps
+// the words in registers).
+__device__ __forceinline__ uint32_t field16(const uint32_t (&w)[4], int j) {
+  const uint32_t x = j < 2 ? w[0] : (j < 4 ? w[1] : (j < 6 ? w[2] : w[3]));
+  return (x >> ((j & 1) * 16)) & 0xFFFFu;
+}
+
+// Inclusive warp scan of four words of packed 16-bit counts.
+__device__ __forceinline__ void warp_scan4(uint32_t (&w)[4]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, w[i], o);
+      if (lane >= o) w[i] += y;
+    }
+  }
+}
+
+// Per-round block offsets from the warps' inclusive round totals in rw[w][half * 4 ...]:
+// base_j = (survivors of rounds before j) + (round j survivors of lower warps) + (round j
+// survivors of lower lanes).  Returns the grand total.
+__device__ __forceinline__ uint32_t round_bases(const uint32_t (*rw)[8], int half,
+                                                const uint32_t (&incl)[4],
+                                                const uint32_t (&own)[4], uint32_t (&base)[4]) {
+  const int warp = threadIdx.x >> 5;
+  uint32_t tot[4] = {0, 0, 0, 0}, pre[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const uint4 v = lds128(&rw[w][half * 4]);
+    const uint32_t x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      tot[i] += x[i];
+      pre[i] += w < warp ? x[i] : 0u;
+    }
+  }
+  uint32_t start = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t b = start + field16(pre, j) + field16(incl, j) - field16(own, j);
+    if (j & 1) base[j >> 1] |= b << 16; else base[j >> 1] = b;
+    start += field16(tot, j);
+  }
+  return start;
+}
+
+// Counts the chunk's survivors under threshold T: key < T (STRICT), key <= T, or every value
+// (take_all, T == kNoThreshold).  TIES (non-strict, not take-all): survivors with key == T are
+// counted apart, so the caller can keep only the first ones by index.  One barrier.
+template <bool STRICT, bool TIES>
+__device__ __forceinline__ SCount strided_count(const StageInfo& si, const uint8_t* buf,
+                                                LargeScratch& sm, uint32_t T, int& par) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const bool take_all = K == kNoThreshold;
-  const uint32_t vb = key_to_bits(K);
+  const bool take_all = T == kNoThreshold;
+  const uint32_t vb = key_to_bits(T);
   const h2t v2 = u32_as_h2(vb | (vb << 16));
-  LCount c;
-  c.flags = thread_flags<STRICT, true>(si, buf, v2, take_all, &c.cnt);
-  uint32_t incl = 0;
-  if (__ballot_sync(0xFFFFFFFFu, c.cnt != 0)) {
-    incl = c.cnt;
+  SCount c;
+  c.M = 0;
+  c.E = 0;
+  uint32_t own[4] = {0, 0, 0, 0}, owne[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-      if (lane >= o) incl += y;
+  for (int j = 0; j < kVecPerThread; ++j) {
+    const int vi = j * kThreads + tid;
+    if (vi < si.nvc) {
+      const uint4 w = lds128(buf + vi * 16);
+      uint32_t m, e = 0;
+      if (TIES) {
+        const uint32_t lt = gt_mask8(w, v2);  // value > V: key < T
+        m = ge_mask8(w, v2);                  // value >= V: key <= T
+        e = m & ~lt;
+      } else {
+        m = take_all ? 0xFFu : pass_mask8<STRICT>(w, v2);
+      }
+      if (vi == si.vlo || vi == si.vhi) {
+        const uint32_t vm = valid_mask8(si.cv0 + vi, si.a0, si.a1);
+        m &= vm;
+        e &= vm;
+      }
+      c.M |= static_cast<uint64_t>(m) << (8 * j);
+      c.E |= static_cast<uint64_t>(e) << (8 * j);
+      const uint32_t cl = static_cast<uint32_t>(__popc(m & ~e));
+      own[j >> 1] |= cl << ((j & 1) * 16);
+      if (TIES) owne[j >> 1] |= static_cast<uint32_t>(__popc(e)) << ((j & 1) * 16);
     }
   }
-  if (lane == 31) sm.wcnt[par][warp] = incl;
+  uint32_t incl[4] = {own[0], own[1], own[2], own[3]};
+  uint32_t incle[4] = {owne[0], owne[1], owne[2], owne[3]};
+  if (__ballot_sync(0xFFFFFFFFu, c.M != 0)) {
+    warp_scan4(incl);
+    if (TIES) warp_scan4(incle);
+  }
+  if (lane == 31) {
+    *reinterpret_cast<uint4*>(&sm.rw[par][warp][0]) = make_uint4(incl[0], incl[1], incl[2], incl[3]);
+    if (TIES) {
+      *reinterpret_cast<uint4*>(&sm.rw[par][warp][4]) =
+          make_uint4(incle[0], incle[1], incle[2], incle[3]);
+    }
+  }
   csync();
   c.fail = sm.fail != 0;
-  const uint4 wa = lds128(&sm.wcnt[par][0]);
-  const uint4 wb = lds128(&sm.wcnt[par][4]);
-  const uint32_t t[kWarps] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-  uint32_t total = 0, wpre = 0;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    wpre += w < warp ? t[w] : 0u;
-    total += t[w];
-  }
-  c.total = total;
-  c.base = wpre + incl - c.cnt;
+  c.total = round_bases(sm.rw[par], 0, incl, own, c.base);
+  c.total_eq = 0;
+  if (TIES) c.total_eq = round_bases(sm.rw[par], 1, incle, owne, c.ebase);
   par ^= 1;
   return c;
 }
 
-__device__ __forceinline__ LCount count_under(const StageInfo& si, const uint8_t* buf,
-                                              LargeScratch& sm, uint32_t K, bool strict,
-                                              int& par) {
-  return strict ? large_count<true>(si, buf, sm, K, par) : large_count<false>(si, buf, sm, K, par);
-}
-
-// Appends the counted candidates (in index order) at sm.cache[nbuf ...].
-__device__ __forceinline__ void large_append(const StageInfo& si, const uint8_t* buf,
-                                             const LCount& c, uint32_t K, bool strict,
-                                             LargeScratch& sm, uint32_t nbuf) {
-  const bool take_all = K == kNoThreshold;
-  const uint32_t vb = key_to_bits(K);
-  const h2t v2 = u32_as_h2(vb | (vb << 16));
-  if (c.total >= 512) {  // clustered survivors: spread the writes over the block
-    if (strict) write_balanced<true>(si, buf, c.flags, v2, take_all, c.base, c.total, sm, nbuf);
-    else write_balanced<false>(si, buf, c.flags, v2, take_all, c.base, c.total, sm, nbuf);
-  } else if (c.flags) {
-    if (strict) write_flagged<true>(si, buf, c.flags, v2, take_all, c.base, sm, nbuf);
-    else write_flagged<false>(si, buf, c.flags, v2, take_all, c.base, sm, nbuf);
+// Appends the counted survivors at sm.cache[nbuf ...] in index order.  Tie mode keeps every
+// survivor with key < T and the first `need` with key == T.  Each thread visits only its set
+// bits, and in tie mode skips the rounds that hold nothing it still keeps.
+template <bool TIES>
+__device__ __forceinline__ void strided_append(const StageInfo& si, const uint8_t* buf,
+                                               const SCount& c, uint32_t need, LargeScratch& sm,
+                                               uint32_t nbuf) {
+  const int tid = threadIdx.x;
+  const long long e0 = si.cv0 * 8;
+  unsigned long long* out = sm.cache + nbuf;
+#pragma unroll 1
+  for (int j = 0; j < kVecPerThread; ++j) {
+    uint32_t m = static_cast<uint32_t>(c.M >> (8 * j)) & 0xFFu;
+    const uint32_t em = static_cast<uint32_t>(c.E >> (8 * j)) & 0xFFu;
+    uint32_t lpos = field16(c.base, j);
+    uint32_t epos = TIES ? field16(c.ebase, j) : 0u;
+    if (TIES && epos >= need) m &= ~em;  // every tie of this round is past the first `need`
+    if (m == 0) continue;
+    const int vi = j * kThreads + tid;
+    const uint4 w = lds128(buf + vi * 16);
+    // key < T survivors and the ties in front of them, in element order
+    for (uint32_t f = m; f; f &= f - 1) {
+      const int e = __ffs(f) - 1;
+      const uint32_t lidx = static_cast<uint32_t>(vi * 8 + e);
+      const unsigned long long comp = make_composite((vec_half(w, e) << 16) | lidx, e0, si.a0);
+      if (TIES && ((em >> e) & 1u)) {
+        // ties ahead of this one: epos plus those of this vector below element e
+        const uint32_t r = epos + static_cast<uint32_t>(__popc(em & ((1u << e) - 1u)));
+        if (r < need) out[lpos + static_cast<uint32_t>(__popc(m & ~em & ((1u << e) - 1u))) + r] = comp;
+      } else {
+        const uint32_t lt_before = static_cast<uint32_t>(__popc(m & ~em & ((1u << e) - 1u)));
+        uint32_t r = 0;
+        if (TIES) {
+          r = epos + static_cast<uint32_t>(__popc(em & ((1u << e) - 1u)));
+          r = r < need ? r : need;
+        }
+        out[lpos + lt_before + r] = comp;
+      }
+    }
   }
   csync();  // the appended entries are visible to the whole block
+}
+
+// Exact cutoff of the survivors counted in c: the k-th smallest key among them and the number
+// of survivors with a smaller key (two 8-bit digit histograms over the survivors only).
+// Requires c.total + c.total_eq >= k.  The histograms are zero on entry and left zero.
+__device__ __forceinline__ uint32_t survivor_cutoff(const uint8_t* buf, const SCount& c,
+                                                    uint32_t k, LargeScratch& sm,
+                                                    uint32_t* before) {
+  const int tid = threadIdx.x;
+  RunHist rh;
+#pragma unroll 1
+  for (int j = 0; j < kVecPerThread; ++j) {
+    const uint32_t m = static_cast<uint32_t>(c.M >> (8 * j)) & 0xFFu;
+    if (m == 0) continue;
+    const uint4 w = lds128(buf + (j * kThreads + tid) * 16);
+    for (uint32_t f = m; f; f &= f - 1) rh.add(sm.hist1, desc_key(vec_half(w, __ffs(f) - 1)) >> 8);
+  }
+  rh.flush(sm.hist1);
+  csync();
+  if (tid < 32) warp_find_bin(sm.hist1, 0, k, &sm.bin1, &sm.before1);
+  csync();
+  const uint32_t b1 = static_cast<uint32_t>(sm.bin1);
+#pragma unroll 1
+  for (int j = 0; j < kVecPerThread; ++j) {
+    const uint32_t m = static_cast<uint32_t>(c.M >> (8 * j)) & 0xFFu;
+    if (m == 0) continue;
+    const uint4 w = lds128(buf + (j * kThreads + tid) * 16);
+    for (uint32_t f = m; f; f &= f - 1) {
+      const uint32_t key = desc_key(vec_half(w, __ffs(f) - 1));
+      if ((key >> 8) == b1) rh.add(sm.hist2, key & 0xFFu);
+    }
+  }
+  rh.flush(sm.hist2);
+  csync();
+  if (tid < 32) warp_find_bin(sm.hist2, sm.before1, k, &sm.bin2, &sm.before2);
+  csync();
+  const uint32_t kk = (b1 << 8) | static_cast<uint32_t>(sm.bin2);
+  *before = sm.before2;
+  sm.hist1[tid] = 0;
+  sm.hist2[tid] = 0;
+  csync();
+  return kk;
 }
 
 // Cuts the cache to its exact k best (keys below the k-th key, then the first ties at it by
@@ -142,83 +286,289 @@ __device__ uint32_t large_exact(const TopkParams& p, const StageInfo& si, const 
   return kstar;
 }
 
+// ---- contiguous count and append ------------------------------------------------------
+//
+// The steady-state form: thread t owns vectors 8t .. 8t+7, one warp scan and one barrier give
+// every thread its first output position, and each thread writes its own survivors.  That is
+// cheapest while survivors are few and spread; when one thread holds many (survivors clustered
+// in a stretch of the chunk), the strided form above spreads the writes instead.
+struct CCount {
+  uint32_t flags, cnt, base, total, maxcnt;
+  bool fail;
+};
+
+template <bool STRICT>
+__device__ __forceinline__ CCount contig_count(const StageInfo& si, const uint8_t* buf,
+                                               LargeScratch& sm, uint32_t K, int& par) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const uint32_t vb = key_to_bits(K);
+  const h2t v2 = u32_as_h2(vb | (vb << 16));
+  CCount c;
+  c.flags = thread_flags<STRICT, true>(si, buf, v2, false, &c.cnt);
+  uint32_t incl = 0, wmax = 0;
+  if (__ballot_sync(0xFFFFFFFFu, c.cnt != 0)) {
+    incl = c.cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    wmax = __reduce_max_sync(0xFFFFFFFFu, c.cnt);
+  }
+  if (lane == 31) sm.wcnt[par][warp] = incl | (wmax << 16);  // total <= 16384, max <= 64
+  csync();
+  c.fail = sm.fail != 0;
+  const uint4 wa = lds128(&sm.wcnt[par][0]);
+  const uint4 wb = lds128(&sm.wcnt[par][4]);
+  const uint32_t t[kWarps] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+  uint32_t total = 0, wpre = 0, mx = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const uint32_t tw = t[w] & 0xFFFFu;
+    wpre += w < warp ? tw : 0u;
+    total += tw;
+    mx = (t[w] >> 16) > mx ? (t[w] >> 16) : mx;
+  }
+  c.total = total;
+  c.maxcnt = mx;
+  c.base = wpre + incl - c.cnt;
+  par ^= 1;
+  return c;
+}
+
+// Writes this thread's survivors under K (key < K with STRICT, else key <= K; flagged
+// vectors, index order) at sm.cache[nbuf + base ...].
+template <bool STRICT>
+__device__ __forceinline__ void contig_append(const StageInfo& si, const uint8_t* buf,
+                                              const CCount& c, uint32_t K, LargeScratch& sm,
+                                              uint32_t nbuf) {
+  const int tid = threadIdx.x;
+  const uint32_t vb = key_to_bits(K);
+  const h2t v2 = u32_as_h2(vb | (vb << 16));
+  const long long e0 = si.cv0 * 8;
+  unsigned long long* out = sm.cache + nbuf + c.base;
+  uint32_t r = 0;
+  for (uint32_t flags = c.flags; flags; flags &= flags - 1) {
+    const int j = __ffs(flags) - 1;
+    const int vi = tid * kVecPerThread + j;
+    const uint4 w = lds128(buf + vi * 16);
+    uint32_t m = pass_mask8<STRICT>(w, v2);
+    if (vi == si.vlo || vi == si.vhi) m &= valid_mask8(si.cv0 + vi, si.a0, si.a1);
+    for (; m; m &= m - 1) {
+      const int e = __ffs(m) - 1;
+      const uint32_t lidx = static_cast<uint32_t>(vi * 8 + e);
+      out[r++] = make_composite((vec_half(w, e) << 16) | lidx, e0, si.a0);
+    }
+  }
+  csync();
+}
+
+// A thread holding more survivors than this writes too long alone: the strided form is used.
+constexpr uint32_t kClusterMax = 16;
+
+// Appends this chunk's exact top k among the survivors counted in t (survivors under a
+// threshold certified for this chunk, at least k of them): the k-th smallest survivor key T2
+// (t's own threshold when fewer than k survivors beat it, else a digit select over the
+// survivors), every survivor with key < T2 and the first ties at T2 by index.  The cache first
+// drops what these k entries beat and, if still short of room, is cut to its own k best.
+// Afterwards T2 is the segment's strict threshold.  Returns false when a wait failed.
+__device__ bool append_chunk_topk(const StageInfo& si, const uint8_t* buf, SCount& t, uint32_t T,
+                                  bool tie_counted, LargeScratch& sm, LargeState& ls,
+                                  uint32_t k, int& par) {
+  constexpr uint32_t C = Cfg<true>::kCacheCap;
+  uint32_t T2 = T;
+  if (!tie_counted || t.total >= k) {
+    uint32_t before;
+    T2 = survivor_cutoff(buf, t, k, sm, &before);
+    if (T2 == kNoThreshold) return false;  // the k-th survivor is a NaN: the caller's fallback
+    t = strided_count<false, true>(si, buf, sm, T2, par);
+    if (t.fail) return false;
+  }
+  const uint32_t need = k - t.total;  // ties at T2 within the chunk's top k
+  if (k > C - ls.nbuf && ls.nbuf > 0) drop_above(sm, ls, T2);
+  if (k > C - ls.nbuf) cut_to_k(sm, ls, k);
+  strided_append<true>(si, buf, t, need, sm, ls.nbuf);
+  ls.nbuf += k;
+  ls.added = 0;
+  ls.quiet = false;
+  if (ls.K == kNoThreshold || T2 < ls.K) ls.K = T2;
+  ls.strict = true;
+  return true;
+}
+
 // One non-empty chunk of the current part.  Returns false when a wait failed (sm.fail).
 __device__ bool large_chunk(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
                             LargeScratch& sm, LargeState& ls, int& par) {
   constexpr uint32_t C = Cfg<true>::kCacheCap;
   const uint32_t k = static_cast<uint32_t>(p.k);
   // A chunk after a quiet one under a strict threshold: the maximum test and one OR-barrier.
-  if (ls.quiet && ls.strict && ls.K < kNoThreshold) {
+  if (ls.quiet && ls.K < kNoThreshold) {
     const uint32_t vb = key_to_bits(ls.K);
     uint32_t cnt;
     const uint32_t f = thread_flags<true>(si, buf, u32_as_h2(vb | (vb << 16)), false, &cnt);
     if (!group_or<kThreads>(f != 0 || sm.fail != 0)) return true;
   }
-  LCount c;
+  // Steady state: survivors under the segment's strict threshold, if the cache has room.
+  SCount c;
   bool counted = false;
   if (ls.K != kNoThreshold && !ls.rising) {
-    c = count_under(si, buf, sm, ls.K, ls.strict, par);
-    if (c.fail) return false;
-    counted = true;
-    if (c.total <= C - ls.nbuf) {
-      large_append(si, buf, c, ls.K, ls.strict, sm, ls.nbuf);
-      ls.nbuf += c.total;
-      ls.added += c.total;
-      ls.quiet = c.total == 0;
-      if (ls.added >= k && ls.nbuf >= k) {  // k more candidates: a tighter threshold
-        const uint32_t kk = buffer_kth_key_block(sm, ls.nbuf, k);
+    const CCount cc = contig_count<true>(si, buf, sm, ls.K, par);
+    if (cc.fail) return false;
+    if (cc.total <= C - ls.nbuf) {
+      if (cc.maxcnt <= kClusterMax) {
+        contig_append<true>(si, buf, cc, ls.K, sm, ls.nbuf);
+      } else {
+        c = strided_count<true, false>(si, buf, sm, ls.K, par);
+        if (c.fail) return false;
+        strided_append<false>(si, buf, c, 0u, sm, ls.nbuf);
+      }
+      ls.nbuf += cc.total;
+      ls.added += cc.total;
+      ls.quiet = cc.total == 0;
+      if (ls.added >= k && ls.nbuf >= k) {  // k more since the last tightening: the cache's
+        const uint32_t kk = buffer_kth_key_block(sm, ls.nbuf, k);  // k-th key is tighter
         if (kk < ls.K) ls.K = kk;
-        ls.strict = true;
         ls.added = 0;
       }
       return true;
     }
+    counted = true;  // the stale threshold overflowed the cache
   }
-  // The threshold this chunk certifies by itself: its k-th best group maximum.
+  // The threshold this chunk certifies by itself: its k-th best group maximum kc (at least k
+  // of its values have key <= kc).
   const uint32_t kc = chunk_select<true>(p, si, buf, sm);
   if (sm.fail) return false;
-  const bool own = kc < ls.K || ls.K == kNoThreshold;  // kc (key <= kc) is the tighter bound
-  ls.rising = counted ? own : (ls.rising && own);
-  uint32_t T = own ? kc : ls.K;
-  bool st = own ? false : ls.strict;
-  if (own && kc != kNoThreshold && ls.nbuf > 0) {
-    // every cache entry with key > kc is beaten by >= k values of this chunk: drop them when
-    // the room is short (rising rows lose their whole cache here)
-    if (ls.nbuf > C - k) drop_above(sm, ls, kc);
-  }
-  if (own || !counted) {  // otherwise T is the threshold just counted
-    c = count_under(si, buf, sm, T, st, par);
-    if (c.fail) return false;
-  }
-  if (c.total > C - ls.nbuf && ls.nbuf > k) {
-    cut_to_k(sm, ls, k);  // room for at least k more
-    if (ls.K < T || (ls.K == T && !st)) {
-      T = ls.K;
-      st = true;
-      c = count_under(si, buf, sm, T, st, par);
-      if (c.fail) return false;
-    }
-  }
-  if (c.total <= C - ls.nbuf) {
-    large_append(si, buf, c, T, st, sm, ls.nbuf);
-    ls.nbuf += c.total;
-    ls.added += c.total;
-    ls.quiet = c.total == 0;
-    if (T != kNoThreshold && (c.total > 0 || st)) {
-      // T is certified: by this chunk (kc: >= k values with key <= kc, all written now), or it
-      // is the segment's own strict threshold
-      if (T < ls.K || ls.K == kNoThreshold) ls.K = T;
+  const bool own = kc != kNoThreshold && (ls.K == kNoThreshold || kc < ls.K);
+  ls.rising = (counted || ls.rising) && own;  // values ramp up: skip the stale count next time
+  // Every value with key <= kc, when the cache has room for them (the usual first chunk).
+  // With less room than about k (rising rows after their first chunk) that seldom fits, and
+  // the exact top k below is taken directly.
+  if (own && C - ls.nbuf >= k + k / 8) {
+    const CCount cc = contig_count<false>(si, buf, sm, kc, par);
+    if (cc.fail) return false;
+    if (cc.total <= C - ls.nbuf) {
+      if (cc.maxcnt <= kClusterMax) {
+        contig_append<false>(si, buf, cc, kc, sm, ls.nbuf);
+      } else {
+        c = strided_count<false, false>(si, buf, sm, kc, par);
+        if (c.fail) return false;
+        strided_append<false>(si, buf, c, 0u, sm, ls.nbuf);
+      }
+      ls.nbuf += cc.total;
+      ls.added = 0;
+      ls.quiet = false;
+      ls.K = kc;  // certified: >= k values with key <= kc are in the cache now
       ls.strict = true;
+      return true;
     }
-  } else {
-    // more ties at the chunk's threshold than the cache has room for: exact top k of the chunk
-    const uint32_t kstar = large_exact(p, si, buf, sm, ls, T, st);
-    if (kstar < ls.K || ls.K == kNoThreshold) ls.K = kstar;
-    ls.strict = true;
-    ls.added = 0;
-    ls.quiet = false;
   }
+  if (own) {
+    // too many (heavy ties, or a loose kc): the chunk's exact top k
+    c = strided_count<false, true>(si, buf, sm, kc, par);
+    if (c.fail) return false;
+    if (append_chunk_topk(si, buf, c, kc, true, sm, ls, k, par)) return true;
+    if (sm.fail) return false;
+  } else {
+    // kc is no better than the segment's threshold (or there is neither): survivors under
+    // that threshold, or every value
+    c = ls.K == kNoThreshold ? strided_count<false, false>(si, buf, sm, kNoThreshold, par)
+                             : strided_count<true, false>(si, buf, sm, ls.K, par);
+    if (c.fail) return false;
+    if (c.total > C - ls.nbuf && ls.nbuf > k) {
+      const uint32_t K1 = ls.K;
+      cut_to_k(sm, ls, k);
+      if (ls.K != K1) {
+        c = strided_count<true, false>(si, buf, sm, ls.K, par);
+        if (c.fail) return false;
+      }
+    }
+    if (c.total <= C - ls.nbuf) {
+      strided_append<false>(si, buf, c, 0u, sm, ls.nbuf);
+      ls.nbuf += c.total;
+      ls.quiet = c.total == 0;
+      return true;
+    }
+    if (append_chunk_topk(si, buf, c, ls.K, false, sm, ls, k, par)) return true;
+    if (sm.fail) return false;
+  }
+  // The chunk's k-th best is a NaN (fewer than k numbers in it): the ordered exact select,
+  // which places NaNs by index.
+  if (ls.nbuf > C - k) cut_to_k(sm, ls, k);
+  const uint32_t T = own ? kc : ls.K;
+  const bool st = !own && ls.K != kNoThreshold;
+  const uint32_t kstar = large_exact(p, si, buf, sm, ls, T, st);
+  if (ls.K == kNoThreshold || kstar < ls.K) ls.K = kstar;
+  ls.strict = true;
+  ls.quiet = false;
   return true;
+}
+
+// ---- row output ----------------------------------------------------------------------
+
+// Writes row s from the n <= k composites at sm.cache[0 .. n): in ascending composite order
+// (key, then index: the reference's order, include/batch_topk_types.cuh:50-92) as value bits
+// and indices; slots n .. k-1 get the padding (-inf, index -1).  Warp w sorts entries
+// [128 w, 128 w + 128) in registers (bitonic, 4 a lane); then every entry's rank is its place
+// in its own run plus, per other run, a binary search for the entries below it, and it is
+// written straight to that slot of the row.
+__device__ void sort_emit(const TopkParams& p, LargeScratch& sm, uint32_t n, int s,
+                          long long len) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const uint32_t warp = static_cast<uint32_t>(tid >> 5);
+  const uint32_t k = static_cast<uint32_t>(p.k);
+  const uint32_t runs = (n + 127) / 128;  // <= 8 runs of 128 (n <= k <= 1024)
+  unsigned long long x[4];
+  if (warp < runs) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const uint32_t i = warp * 128 + r * 32 + lane;
+      x[r] = i < n ? sm.cache[i] : ~0ull;
+    }
+    warp_sort_regs<4>(x);  // element r * 32 + lane of the run in x[r]
+  }
+  csync();
+  if (warp < runs) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) sm.cache[warp * 128 + r * 32 + lane] = x[r];
+  }
+  csync();
+  uint16_t* ov = p.out_values + static_cast<long long>(s) * k;
+  int* oi = p.out_indices + static_cast<long long>(s) * k;
+  if (warp < runs) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const unsigned long long v = x[r];
+      if (v == ~0ull) continue;  // padding past n
+      uint32_t rank = static_cast<uint32_t>(r * 32 + lane);
+      for (uint32_t q = 0; q < runs; ++q) {
+        if (q == warp) continue;
+        const unsigned long long* run = sm.cache + q * 128;
+        uint32_t lo = 0;  // entries of run q below v (composites are distinct)
+#pragma unroll
+        for (uint32_t step = 128; step > 0; step >>= 1) {
+          if (lo + step <= 128 && run[lo + step - 1] < v) lo += step;
+        }
+        rank += lo;
+      }
+      if (rank < k) {
+        ov[rank] = static_cast<uint16_t>(v & 0xFFFFu);
+        oi[rank] = static_cast<int>((v >> 16) & 0xFFFFFFFFu);
+      }
+    }
+  }
+  for (uint32_t r = n + tid; r < k; r += kThreads) {
+    ov[r] = kNegInfBits;
+    oi[r] = -1;
+  }
+  if (tid == 0) {
+    // fewer than k candidates can only come from a segment shorter than k
+    if (n < k && len >= static_cast<long long>(k)) atomicOr(&p.status[0], kStatusCertifyFailed);
+    if (p.stats) atomicAdd(&p.status[4], 1u);
+  }
+  csync();  // the cache is free again
 }
 
 // Loads n composites from a partial list in global memory into sm.cache[at ...].
@@ -235,8 +585,8 @@ __device__ void large_close(const TopkParams& p, LargeState& ls, LargeScratch& s
   const uint32_t k = static_cast<uint32_t>(p.k);
   const long long len = ls.a1 - ls.a0;
   if (ls.mycnt == ls.nchunks) {
-    CacheSrc cs{sm.cache};
-    select_and_emit<true>(p, cs, ls.nbuf, 0xFFFFu, ls.s, len, sm);
+    if (ls.nbuf > k) cut_to_k(sm, ls, k);
+    sort_emit(p, sm, ls.nbuf, ls.s, len);
     return;
   }
   // split segment: this part's exact top k, in index order, to its first slot
@@ -278,8 +628,9 @@ __device__ void large_close(const TopkParams& p, LargeState& ls, LargeScratch& s
     }
     csync();  // tbase is rewritten by the next round
   }
-  CacheSrc cs{sm.cache};
-  select_and_emit<true>(p, cs, n, 0xFFFFu, ls.s, len, sm);
+  ls.nbuf = n;
+  if (ls.nbuf > k) cut_to_k(sm, ls, k);
+  sort_emit(p, sm, ls.nbuf, ls.s, len);
 }
 
 __device__ void consumer_loop_large(const TopkParams& p, uint8_t* stages, uint64_t* full,
