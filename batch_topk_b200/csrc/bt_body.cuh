@@ -275,22 +275,23 @@ __device__ uint32_t buffer_kth_key_block(Scratch<BIG>& sm, uint32_t n, uint32_t 
 // cutoff key; *S gets this thread's selected elements (bit 8*j+e), *sbase their first output
 // position and *stot the block total (== k).  Rare path.
 
-// Calls f(bits, pos) for every candidate of this thread (bit pos of M, pos = 8 * vector +
-// element; bits = the value's 16-bit pattern).  The thread's vectors are read whole, rotated so a quarter-warp's loads cover all
-// banks; with ORDERED the vectors are visited in index order instead (for tie placement).
-template <bool ORDERED, class F>
-__device__ __forceinline__ void for_each_candidate(const uint8_t* buf, uint64_t M, F&& f) {
+// Writes this thread's selected elements (bit 8 j + e of S: element e of its vector j), in
+// index order, as (key, index, bits) composites at out[0 ...]; e0 is the chunk's first aligned
+// element, a0 the segment's.  A plain loop (no lambda capturing the running count, which
+// would keep it in local memory).
+__device__ __forceinline__ void write_selected(const uint8_t* buf, uint64_t S, long long e0,
+                                               long long a0, unsigned long long* out) {
   const int tid = threadIdx.x;
-  const int sw = ORDERED ? 0 : (tid & 7);
+  uint32_t r = 0;
 #pragma unroll 1
-  for (int jj = 0; jj < kVecPerThread; ++jj) {
-    const int j = jj ^ sw;
-    const uint32_t m8 = static_cast<uint32_t>(M >> (8 * j)) & 0xFFu;
+  for (int j = 0; j < kVecPerThread; ++j) {
+    uint32_t m8 = static_cast<uint32_t>(S >> (8 * j)) & 0xFFu;
     if (m8 == 0) continue;
     const uint4 w = lds128(buf + (tid * kVecPerThread + j) * 16);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      if (m8 & (1u << e)) f(vec_half(w, e), 8 * j + e);
+    for (; m8; m8 &= m8 - 1) {
+      const int e = __ffs(m8) - 1;
+      const uint32_t lidx = static_cast<uint32_t>(tid * 64 + 8 * j + e);
+      out[r++] = make_composite((vec_half(w, e) << 16) | lidx, e0, a0);
     }
   }
 }
@@ -312,42 +313,66 @@ __device__ uint32_t exact_local_select(const TopkParams& p, const StageInfo& si,
       M |= static_cast<uint64_t>(m) << (8 * j);
     }
   }
-  RunHist rh;
-  for_each_candidate<false>(buf, M, [&](uint32_t bits, int) {
-    rh.add(sm.hist1, desc_key(bits) >> 8);
-  });
-  rh.flush(sm.hist1);
+  // The candidate passes walk all 64 element positions of the thread in the same order in
+  // every lane, with predicated shared atomics: lane-dependent loops over set bits diverged,
+  // and warp-aggregated adds (match_any, or a ballot for the first lane's bin) cost more than
+  // the atomics they saved.
+  const int sw = tid & 7;  // rotated vector order: a quarter-warp's 16-byte loads hit all banks
+#pragma unroll 1
+  for (int jj = 0; jj < kVecPerThread; ++jj) {
+    const int j = jj ^ sw;
+    const uint32_t m8 = static_cast<uint32_t>(M >> (8 * j)) & 0xFFu;
+    const uint4 w = lds128(buf + (tid * kVecPerThread + j) * 16);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if ((m8 >> e) & 1u) atomicAdd(&sm.hist1[desc_key(vec_half(w, e)) >> 8], 1u);
+    }
+  }
   csync();
   if (tid < 32) warp_find_bin(sm.hist1, 0, p.k, &sm.bin1, &sm.before1);
   csync();
   const uint32_t b1 = static_cast<uint32_t>(sm.bin1);
-  for_each_candidate<false>(buf, M, [&](uint32_t bits, int) {
-    const uint32_t key = desc_key(bits);
-    if ((key >> 8) == b1) rh.add(sm.hist2, key & 0xFFu);
-  });
-  rh.flush(sm.hist2);
+#pragma unroll 1
+  for (int jj = 0; jj < kVecPerThread; ++jj) {
+    const int j = jj ^ sw;
+    const uint32_t m8 = static_cast<uint32_t>(M >> (8 * j)) & 0xFFu;
+    const uint4 w = lds128(buf + (tid * kVecPerThread + j) * 16);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t key = desc_key(vec_half(w, e));
+      if (((m8 >> e) & 1u) && (key >> 8) == b1) atomicAdd(&sm.hist2[key & 0xFFu], 1u);
+    }
+  }
   csync();
   if (tid < 32) warp_find_bin(sm.hist2, sm.before1, p.k, &sm.bin2, &sm.before2);
   csync();
   const uint32_t kstar = (b1 << 8) | static_cast<uint32_t>(sm.bin2);
   const uint32_t need = static_cast<uint32_t>(p.k) - sm.before2;
-  uint32_t tcnt = 0;
-  for_each_candidate<false>(buf, M, [&](uint32_t bits, int) {
-    tcnt += desc_key(bits) == kstar ? 1u : 0u;
-  });
-  uint32_t ttot;
-  const uint32_t tbase = block_excl_scan<kThreads, true>(tcnt, &ttot, sm.warp_tot);
-  uint64_t S = 0;
-  uint32_t tr = tbase;
-  for_each_candidate<true>(buf, M, [&](uint32_t bits, int pos) {  // index order: ties by index
-    const uint32_t key = desc_key(bits);
-    if (key < kstar) {
-      S |= 1ull << pos;
-    } else if (key == kstar) {
-      if (tr < need) S |= 1ull << pos;
-      ++tr;
+  // keys below the cutoff, and this thread's ties at it, in index order
+  uint64_t S = 0, T = 0;
+#pragma unroll 1
+  for (int jj = 0; jj < kVecPerThread; ++jj) {
+    const int j = jj ^ sw;
+    const uint32_t m8 = static_cast<uint32_t>(M >> (8 * j)) & 0xFFu;
+    const uint4 w = lds128(buf + (tid * kVecPerThread + j) * 16);
+    uint32_t lt = 0, eq = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t key = desc_key(vec_half(w, e));
+      lt |= static_cast<uint32_t>(key < kstar) << e;
+      eq |= static_cast<uint32_t>(key == kstar) << e;
     }
-  });
+    S |= static_cast<uint64_t>(lt & m8) << (8 * j);
+    T |= static_cast<uint64_t>(eq & m8) << (8 * j);
+  }
+  uint32_t ttot;
+  const uint32_t tbase = block_excl_scan<kThreads, true>(static_cast<uint32_t>(__popcll(T)), &ttot,
+                                                         sm.warp_tot);
+  // the ties ranked below `need` by index join the selection
+  for (uint32_t tr = tbase; T != 0 && tr < need; ++tr) {
+    S |= T & (~T + 1);  // lowest remaining tie
+    T &= T - 1;
+  }
   *sbase_out =
       block_excl_scan<kThreads, true>(static_cast<uint32_t>(__popcll(S)), stot_out, sm.warp_tot);
   *S_out = S;

@@ -264,15 +264,6 @@ __device__ __forceinline__ void warp_find_bin(const uint32_t* hist, uint32_t bas
   }
 }
 
-// Histogram add of one value per lane, aggregated across equal bins in the warp.
-__device__ __forceinline__ void hist_add_match(uint32_t* hist, uint32_t bin, bool active) {
-  const uint32_t b = active ? bin : 0xFFFFFFFFu;
-  const uint32_t peers = __match_any_sync(0xFFFFFFFFu, b);
-  if (active && (threadIdx.x & 31) == static_cast<unsigned>(__ffs(peers) - 1)) {
-    atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
-  }
-}
-
 // Per-thread run-length aggregation of histogram adds (for sequential scans where equal
 // bins cluster, e.g. tie-heavy or sorted data).
 struct RunHist {

@@ -208,16 +208,18 @@ __device__ __forceinline__ void strided_append(const StageInfo& si, const uint8_
 __device__ __forceinline__ uint32_t survivor_cutoff(const uint8_t* buf, const SCount& c,
                                                     uint32_t k, LargeScratch& sm,
                                                     uint32_t* before) {
+  // Every lane walks all 64 of its element positions in the same order, with predicated
+  // shared atomics (lane-dependent loops over set bits diverge).
   const int tid = threadIdx.x;
-  RunHist rh;
 #pragma unroll 1
   for (int j = 0; j < kVecPerThread; ++j) {
     const uint32_t m = static_cast<uint32_t>(c.M >> (8 * j)) & 0xFFu;
-    if (m == 0) continue;
     const uint4 w = lds128(buf + (j * kThreads + tid) * 16);
-    for (uint32_t f = m; f; f &= f - 1) rh.add(sm.hist1, desc_key(vec_half(w, __ffs(f) - 1)) >> 8);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if ((m >> e) & 1u) atomicAdd(&sm.hist1[desc_key(vec_half(w, e)) >> 8], 1u);
+    }
   }
-  rh.flush(sm.hist1);
   csync();
   if (tid < 32) warp_find_bin(sm.hist1, 0, k, &sm.bin1, &sm.before1);
   csync();
@@ -225,14 +227,13 @@ __device__ __forceinline__ uint32_t survivor_cutoff(const uint8_t* buf, const SC
 #pragma unroll 1
   for (int j = 0; j < kVecPerThread; ++j) {
     const uint32_t m = static_cast<uint32_t>(c.M >> (8 * j)) & 0xFFu;
-    if (m == 0) continue;
     const uint4 w = lds128(buf + (j * kThreads + tid) * 16);
-    for (uint32_t f = m; f; f &= f - 1) {
-      const uint32_t key = desc_key(vec_half(w, __ffs(f) - 1));
-      if ((key >> 8) == b1) rh.add(sm.hist2, key & 0xFFu);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t key = desc_key(vec_half(w, e));
+      if (((m >> e) & 1u) && (key >> 8) == b1) atomicAdd(&sm.hist2[key & 0xFFu], 1u);
     }
   }
-  rh.flush(sm.hist2);
   csync();
   if (tid < 32) warp_find_bin(sm.hist2, sm.before1, k, &sm.bin2, &sm.before2);
   csync();
@@ -269,18 +270,11 @@ __device__ __forceinline__ void drop_above(LargeScratch& sm, LargeState& ls, uin
 // threshold leaves more candidates than the cache has room for (heavy ties at it).
 __device__ uint32_t large_exact(const TopkParams& p, const StageInfo& si, const uint8_t* buf,
                                 LargeScratch& sm, LargeState& ls, uint32_t T, bool strict) {
-  const int tid = threadIdx.x;
   uint64_t S;
   uint32_t sbase, stot;
   const uint32_t kstar = exact_local_select(p, si, buf, sm, T, strict, &S, &sbase, &stot);
   const long long e0 = si.cv0 * 8;
-  uint32_t r = 0;
-  const uint32_t at = ls.nbuf + sbase;
-  for_each_candidate<true>(buf, S, [&](uint32_t bits, int pos) {
-    const uint32_t w = (bits << 16) | static_cast<uint32_t>(tid * 64 + pos);
-    sm.cache[at + r] = make_composite(w, e0, si.a0);
-    ++r;
-  });
+  write_selected(buf, S, e0, si.a0, sm.cache + ls.nbuf + sbase);
   ls.nbuf += stot;
   csync();
   return kstar;

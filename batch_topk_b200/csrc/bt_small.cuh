@@ -178,13 +178,7 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
       uint32_t sbase, stot;
       const uint32_t kstar = exact_local_select(p, si, buf, sm, K, strict, &S, &sbase, &stot);
       if (!wait_batch_free(p, sm, nb)) sm.fail = 1u;  // caught at the next barrier
-      const int tid = threadIdx.x;
-      const long long e0 = si.cv0 * 8;
-      uint32_t r = 0;
-      for_each_candidate<true>(buf, S, [&](uint32_t bits, int pos) {
-        const uint32_t lidx = static_cast<uint32_t>(tid * 64 + pos);
-        sm.batch[b][sbase + r++] = make_composite((bits << 16) | lidx, e0, si.a0);
-      });
+      write_selected(buf, S, si.cv0 * 8, si.a0, sm.batch[b] + sbase);
       K = kstar;
       strict = true;
       n = stot;
