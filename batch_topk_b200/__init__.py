@@ -101,6 +101,32 @@ def batch_topk_bf16_segmented_workspace_size(seg_num: int, max_total_len: int, k
     return int(_lib.load().bt_topk_bf16_segmented_workspace_size(seg_num, max_total_len, k))
 
 
+def batch_topk_f32(d_input: int, seg_num: int, seg_len: int, k: int, d_output_values: int,
+                   d_output_indices: int, d_workspace: int, workspace_bytes: int,
+                   stream: int = 0) -> int:
+    """batch_topk_half for float32 rows (no reference counterpart): 32-bit values in and out
+    (4-byte aligned), the same contract and order (NaN last, -0 == +0, ties by index)."""
+    return _lib.load().bt_topk_f32(d_input, seg_num, seg_len, k, d_output_values,
+                                   d_output_indices, d_workspace, workspace_bytes, stream)
+
+
+def batch_topk_f32_workspace_size(seg_num: int, seg_len: int, k: int) -> int:
+    return int(_lib.load().bt_topk_f32_workspace_size(seg_num, seg_len, k))
+
+
+def batch_topk_f32_segmented(d_input: int, d_offsets: int, seg_num: int, max_total_len: int,
+                             k: int, d_output_values: int, d_output_indices: int,
+                             d_workspace: int, workspace_bytes: int, stream: int = 0) -> int:
+    """CSR variant for float32 values (no reference counterpart); -inf (0xFF800000) pads."""
+    return _lib.load().bt_topk_f32_segmented(d_input, d_offsets, seg_num, max_total_len, k,
+                                             d_output_values, d_output_indices, d_workspace,
+                                             workspace_bytes, stream)
+
+
+def batch_topk_f32_segmented_workspace_size(seg_num: int, max_total_len: int, k: int) -> int:
+    return int(_lib.load().bt_topk_f32_segmented_workspace_size(seg_num, max_total_len, k))
+
+
 def batch_topk_half_noalloc(d_input: int, seg_num: int, seg_len: int, k: int,
                             d_output_values: int, d_output_indices: int, stream: int = 0) -> int:
     """bt_topk_half_noalloc (no reference counterpart): batch_topk_half on the library's fixed

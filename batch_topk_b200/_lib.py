@@ -21,6 +21,10 @@ EXPORTED = (
     "bt_topk_bf16_workspace_size",
     "bt_topk_bf16_segmented",
     "bt_topk_bf16_segmented_workspace_size",
+    "bt_topk_f32",
+    "bt_topk_f32_workspace_size",
+    "bt_topk_f32_segmented",
+    "bt_topk_f32_segmented_workspace_size",
     "bt_workspace_status",
     "bt_noalloc_status",
     "bt_set_handoff_wait_tries",
@@ -67,6 +71,14 @@ def load() -> C.CDLL:
         lib.bt_topk_bf16_segmented.restype = i32
         lib.bt_topk_bf16_segmented_workspace_size.argtypes = [i32, i64, i32]
         lib.bt_topk_bf16_segmented_workspace_size.restype = sz
+        lib.bt_topk_f32.argtypes = [vp, i32, i32, i32, vp, vp, vp, sz, vp]
+        lib.bt_topk_f32.restype = i32
+        lib.bt_topk_f32_workspace_size.argtypes = [i32, i32, i32]
+        lib.bt_topk_f32_workspace_size.restype = sz
+        lib.bt_topk_f32_segmented.argtypes = [vp, vp, i32, i64, i32, vp, vp, vp, sz, vp]
+        lib.bt_topk_f32_segmented.restype = i32
+        lib.bt_topk_f32_segmented_workspace_size.argtypes = [i32, i64, i32]
+        lib.bt_topk_f32_segmented_workspace_size.restype = sz
         lib.bt_workspace_status.argtypes = [vp, i32, vp, C.POINTER(C.c_uint * 6)]
         lib.bt_workspace_status.restype = i32
         lib.bt_noalloc_status.argtypes = [vp, C.POINTER(C.c_uint * 6)]

@@ -16,7 +16,7 @@ SRC = os.path.join(HERE, "csrc", "batch_topk.cu")
 GEN_SRC = os.path.join(HERE, "csrc", "gen.cu")  # device-side input generation
 HEADERS = [os.path.join(HERE, "csrc", f) for f in ("bt_device.cuh", "bt_kernels.cuh", "bt_body.cuh",
                                                    "bt_elem.cuh", "bt_small.cuh",
-                                                   "bt_large.cuh")] + [
+                                                   "bt_large.cuh", "bt_common.cuh", "bt_f32.cuh")] + [
     os.path.join(REPO, "include", "batch_topk_b200.h"),
     os.path.join(REPO, "include", "batch_topk_b200_gen.h"),
 ]

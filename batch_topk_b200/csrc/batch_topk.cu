@@ -23,16 +23,16 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 int groups_for_k(int k) { return k <= 64 ? 1 : (k <= 128 ? 2 : (k <= 256 ? 4 : 8)); }
 int cap_for_k(int k) { return k * 4 < 256 ? 256 : k * 4; }
 
-// Chunk slots one fixed-length segment may need: its 16-byte vectors span at most
-// ceil(len/8) + 1 when the row start is not 16-byte aligned.
-long long slots_per_segment(long long seg_len) {
-  const long long nv = (seg_len + 7) / 8 + 1;
+// Chunk slots one fixed-length segment may need: its 16-byte vectors (epv elements each) span
+// at most ceil(len / epv) + 1 when the row start is not 16-byte aligned.
+long long slots_per_segment(long long seg_len, int epv = 8) {
+  const long long nv = (seg_len + epv - 1) / epv + 1;
   return (nv + kVecPerChunk - 1) / kVecPerChunk;
 }
 
 // Upper bound on chunk slots for a CSR batch of seg_num segments totalling total_len values.
-long long csr_slot_bound(long long seg_num, long long total_len) {
-  return (total_len / 8 + 2 * seg_num) / kVecPerChunk + seg_num + 1;
+long long csr_slot_bound(long long seg_num, long long total_len, int epv = 8) {
+  return (total_len / epv + 2 * seg_num) / kVecPerChunk + seg_num + 1;
 }
 
 struct Layout {
@@ -74,7 +74,10 @@ bool csr_shape_ok(int seg_num, long long max_total_len, int k) {
 
 using TopkKernel = void (*)(TopkParams);
 
-// The streaming kernel for k <= 128 (small) or larger k, per element type.
+// Element types of the entry points: IEEE binary16, bfloat16, binary32.
+enum Elem { kF16 = 0, kBF16 = 1, kF32 = 2 };
+
+// The streaming kernel for k <= 128 (small) or larger k, per 16-bit element type.
 TopkKernel topk_kernel_for(bool big, bool bf16) {
   if (bf16) return big ? bf16::topk_kernel<true> : bf16::topk_kernel<false>;
   return big ? f16::topk_kernel<true> : f16::topk_kernel<false>;
@@ -83,7 +86,7 @@ TopkKernel topk_kernel_for(bool big, bool bf16) {
 struct DeviceInfo {
   bool ready = false;
   int sms = 0;
-  int blocks_per_sm[2] = {0, 0};  // topk_kernel<false>, topk_kernel<true>
+  int blocks_per_sm[3] = {0, 0, 0};  // topk_kernel<false>, topk_kernel<true>, f32::topk_kernel
 };
 
 std::mutex g_mu;
@@ -133,7 +136,15 @@ cudaError_t device_info(DeviceInfo* out) {
       }
       d.blocks_per_sm[big] = best;
     }
-    if (d.blocks_per_sm[0] < 1 || d.blocks_per_sm[1] < 1) return cudaErrorInvalidConfiguration;
+    e = cudaFuncSetAttribute(f32::topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(f32::FLayout::bytes));
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.blocks_per_sm[2], f32::topk_kernel,
+                                                      f32::kBlockThreads, f32::FLayout::bytes);
+    if (e != cudaSuccess) return e;
+    if (d.blocks_per_sm[0] < 1 || d.blocks_per_sm[1] < 1 || d.blocks_per_sm[2] < 1) {
+      return cudaErrorInvalidConfiguration;
+    }
     if (g_stats < 0) {
       const char* s = std::getenv("BT_STATS");
       g_stats = (s && s[0] == '1') ? 1 : 0;
@@ -169,22 +180,22 @@ cudaError_t launch_setup(void (*kernel)(TopkParams), const TopkParams& p, int gr
   return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
-template <bool BIG>
-cudaError_t launch_topk(const TopkParams& p, int grid, bool bf16, cudaStream_t stream) {
+cudaError_t launch_topk(TopkKernel kernel, int threads, size_t smem, const TopkParams& p,
+                        int grid, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(static_cast<unsigned>(block_threads<BIG>()));
-  cfg.dynamicSmemBytes = SmemLayout<BIG>::bytes;
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, topk_kernel_for(BIG, bf16), p);
+  return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
-cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, bool bf16,
+cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, Elem elem,
                             cudaStream_t stream) {
   DeviceInfo di;
   cudaError_t e = device_info(&di);
@@ -194,8 +205,11 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, bool b
     std::lock_guard<std::mutex> lock(g_mu);
     p.handoff_tries = g_handoff_tries;
   }
-  const bool big = p.k > Cfg<false>::kSelCap;
-  const long long resident = static_cast<long long>(di.sms) * di.blocks_per_sm[big ? 1 : 0];
+  // fp32 rows always take the cache kernel; 16-bit rows the merger kernel up to k = 128
+  const bool f32 = elem == kF32;
+  const bool big = f32 || p.k > Cfg<false>::kSelCap;
+  const int kind = f32 ? 2 : (big ? 1 : 0);
+  const long long resident = static_cast<long long>(di.sms) * di.blocks_per_sm[kind];
   p.part_chunks = choose_part_chunks(work_items, p.seg_num, resident);
   long long parts = work_items;  // CSR: an upper bound (every part holds a chunk)
   if (!csr) {
@@ -217,20 +231,32 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, bool b
   const int grid = static_cast<int>(grid_ll);
   p.help_window = p.steal ? (grid < p.seg_num ? grid : p.seg_num) : 0;
   if (g_prof_start) cudaEventRecord(g_prof_start, stream);
-  e = big ? launch_topk<true>(p, grid, bf16, stream) : launch_topk<false>(p, grid, bf16, stream);
+  if (f32) {
+    e = launch_topk(f32::topk_kernel, f32::kBlockThreads, f32::FLayout::bytes, p, grid, stream);
+  } else if (big) {
+    e = launch_topk(topk_kernel_for(true, elem == kBF16), block_threads<true>(),
+                    SmemLayout<true>::bytes, p, grid, stream);
+  } else {
+    e = launch_topk(topk_kernel_for(false, elem == kBF16), block_threads<false>(),
+                    SmemLayout<false>::bytes, p, grid, stream);
+  }
   if (e != cudaSuccess) return e;
   if (g_prof_stop) cudaEventRecord(g_prof_stop, stream);
   return cudaSuccess;
 }
 
+// Elements per 16-byte vector.
+int epv_of(Elem elem) { return elem == kF32 ? 4 : 8; }
+
 TopkParams base_params(const void* d_input, int seg_num, int k, void* d_out_values,
                        int* d_out_indices, void* d_workspace, const Layout& L, long long slots,
-                       bool bf16) {
+                       Elem elem) {
   TopkParams p{};
-  p.pad_bits = bf16 ? 0xFF80u : 0xFC00u;  // -inf
+  p.pad_bits = elem == kF32 ? 0xFF800000u : (elem == kBF16 ? 0xFF80u : 0xFC00u);  // -inf
+  p.epv_shift = elem == kF32 ? 2 : 3;
   const uintptr_t in = reinterpret_cast<uintptr_t>(d_input);
   p.base = reinterpret_cast<const uint16_t*>(in & ~static_cast<uintptr_t>(15));
-  p.shift = static_cast<int>((in & 15) / 2);
+  p.shift = static_cast<int>((in & 15) / (elem == kF32 ? 4 : 2));
   p.seg_num = seg_num;
   p.k = k;
   p.groups = groups_for_k(k);
@@ -246,57 +272,72 @@ TopkParams base_params(const void* d_input, int seg_num, int k, void* d_out_valu
   p.chunk_count = reinterpret_cast<uint32_t*>(ws + L.counts);
   p.chunk_off = reinterpret_cast<uint32_t*>(ws + L.offs);
   p.cand = reinterpret_cast<uint32_t*>(ws + L.cand);
-  p.out_values = static_cast<uint16_t*>(d_out_values);
+  p.out_values = elem == kF32 ? nullptr : static_cast<uint16_t*>(d_out_values);
+  p.out_values32 = elem == kF32 ? static_cast<uint32_t*>(d_out_values) : nullptr;
   p.out_indices = d_out_indices;
   return p;
 }
 
-bool pointers_ok(const void* in, const void* ov, const int* oi, const void* ws) {
+bool pointers_ok(const void* in, const void* ov, const int* oi, const void* ws, Elem elem) {
   if (!in || !ov || !oi || !ws) return false;
   const uintptr_t a = reinterpret_cast<uintptr_t>(in), b = reinterpret_cast<uintptr_t>(ov),
                   c = reinterpret_cast<uintptr_t>(oi), d = reinterpret_cast<uintptr_t>(ws);
-  return (a % 2 == 0) && (b % 2 == 0) && (c % 4 == 0) && (d % 16 == 0);
+  const uintptr_t es = elem == kF32 ? 4 : 2;  // element size: values must be element-aligned
+  return (a % es == 0) && (b % es == 0) && (c % 4 == 0) && (d % 16 == 0);
 }
 
-// Fixed-length rows of 16-bit values (fp16, or bf16 when bf16 is set).
+size_t fixed_workspace(int seg_num, int seg_len, int k, Elem elem) {
+  if (!fixed_shape_ok(seg_num, seg_len, k)) return 0;
+  const long long slots =
+      static_cast<long long>(seg_num) * slots_per_segment(seg_len, epv_of(elem));
+  return make_layout(seg_num, slots, cap_for_k(k), false).total;
+}
+
+size_t csr_workspace(int seg_num, long long max_total_len, int k, Elem elem) {
+  if (!csr_shape_ok(seg_num, max_total_len, k)) return 0;
+  const long long slots = csr_slot_bound(seg_num, max_total_len, epv_of(elem));
+  return make_layout(seg_num, slots, cap_for_k(k), true).total;
+}
+
+// Fixed-length rows of one element type.
 int topk_fixed(const void* d_input, int seg_num, int seg_len, int k, void* d_output_values,
                int* d_output_indices, void* d_workspace, size_t workspace_bytes, void* stream,
-               bool bf16) {
+               Elem elem) {
   if (!fixed_shape_ok(seg_num, seg_len, k)) return cudaErrorInvalidValue;
-  if (!pointers_ok(d_input, d_output_values, d_output_indices, d_workspace)) {
+  if (!pointers_ok(d_input, d_output_values, d_output_indices, d_workspace, elem)) {
     return cudaErrorInvalidValue;
   }
-  const long long p_max = slots_per_segment(seg_len);
+  const long long p_max = slots_per_segment(seg_len, epv_of(elem));
   const long long slots = static_cast<long long>(seg_num) * p_max;
   const Layout L = make_layout(seg_num, slots, cap_for_k(k), false);
   if (workspace_bytes < L.total) return cudaErrorInvalidValue;
   TopkParams p = base_params(d_input, seg_num, k, d_output_values, d_output_indices,
-                             d_workspace, L, slots, bf16);
+                             d_workspace, L, slots, elem);
   p.seg_len = seg_len;
   p.offsets = nullptr;
   p.p_max = static_cast<int>(p_max);
-  return launch_pipeline(p, false, slots, bf16, static_cast<cudaStream_t>(stream));
+  return launch_pipeline(p, false, slots, elem, static_cast<cudaStream_t>(stream));
 }
 
-// CSR batches of 16-bit values (fp16, or bf16 when bf16 is set).
+// CSR batches of one element type.
 int topk_csr(const void* d_input, const int* d_offsets, int seg_num, long long max_total_len,
              int k, void* d_output_values, int* d_output_indices, void* d_workspace,
-             size_t workspace_bytes, void* stream, bool bf16) {
+             size_t workspace_bytes, void* stream, Elem elem) {
   if (!csr_shape_ok(seg_num, max_total_len, k)) return cudaErrorInvalidValue;
   if (!d_offsets || reinterpret_cast<uintptr_t>(d_offsets) % 4 != 0) return cudaErrorInvalidValue;
-  if (!pointers_ok(d_input, d_output_values, d_output_indices, d_workspace)) {
+  if (!pointers_ok(d_input, d_output_values, d_output_indices, d_workspace, elem)) {
     return cudaErrorInvalidValue;
   }
-  const long long slots = csr_slot_bound(seg_num, max_total_len);
+  const long long slots = csr_slot_bound(seg_num, max_total_len, epv_of(elem));
   const Layout L = make_layout(seg_num, slots, cap_for_k(k), true);
   if (workspace_bytes < L.total) return cudaErrorInvalidValue;
   TopkParams p = base_params(d_input, seg_num, k, d_output_values, d_output_indices,
-                             d_workspace, L, slots, bf16);
+                             d_workspace, L, slots, elem);
   p.seg_len = 0;
   p.offsets = d_offsets;
   p.p_max = 0;
   p.max_total_len = max_total_len;
-  return launch_pipeline(p, true, slots, bf16, static_cast<cudaStream_t>(stream));
+  return launch_pipeline(p, true, slots, elem, static_cast<cudaStream_t>(stream));
 }
 
 }  // namespace
@@ -338,15 +379,13 @@ cudaError_t noalloc_scratch(void** out) {
 extern "C" {
 
 size_t bt_topk_half_workspace_size(int seg_num, int seg_len, int k) {
-  if (!bt::fixed_shape_ok(seg_num, seg_len, k)) return 0;
-  const long long slots = static_cast<long long>(seg_num) * bt::slots_per_segment(seg_len);
-  return bt::make_layout(seg_num, slots, bt::cap_for_k(k), false).total;
+  return bt::fixed_workspace(seg_num, seg_len, k, bt::kF16);
 }
 
 int bt_topk_half(const void* d_input, int seg_num, int seg_len, int k, void* d_output_values,
                  int* d_output_indices, void* d_workspace, size_t workspace_bytes, void* stream) {
   return bt::topk_fixed(d_input, seg_num, seg_len, k, d_output_values, d_output_indices,
-                        d_workspace, workspace_bytes, stream, false);
+                        d_workspace, workspace_bytes, stream, bt::kF16);
 }
 
 int bt_topk_half_noalloc(const void* d_input, int seg_num, int seg_len, int k,
@@ -367,9 +406,7 @@ int bt_topk_half_noalloc(const void* d_input, int seg_num, int seg_len, int k,
 }
 
 size_t bt_topk_half_segmented_workspace_size(int seg_num, long long max_total_len, int k) {
-  if (!bt::csr_shape_ok(seg_num, max_total_len, k)) return 0;
-  const long long slots = bt::csr_slot_bound(seg_num, max_total_len);
-  return bt::make_layout(seg_num, slots, bt::cap_for_k(k), true).total;
+  return bt::csr_workspace(seg_num, max_total_len, k, bt::kF16);
 }
 
 int bt_topk_half_segmented(const void* d_input, const int* d_offsets, int seg_num,
@@ -377,7 +414,7 @@ int bt_topk_half_segmented(const void* d_input, const int* d_offsets, int seg_nu
                            int* d_output_indices, void* d_workspace, size_t workspace_bytes,
                            void* stream) {
   return bt::topk_csr(d_input, d_offsets, seg_num, max_total_len, k, d_output_values,
-                      d_output_indices, d_workspace, workspace_bytes, stream, false);
+                      d_output_indices, d_workspace, workspace_bytes, stream, bt::kF16);
 }
 
 size_t bt_topk_bf16_workspace_size(int seg_num, int seg_len, int k) {
@@ -387,7 +424,7 @@ size_t bt_topk_bf16_workspace_size(int seg_num, int seg_len, int k) {
 int bt_topk_bf16(const void* d_input, int seg_num, int seg_len, int k, void* d_output_values,
                  int* d_output_indices, void* d_workspace, size_t workspace_bytes, void* stream) {
   return bt::topk_fixed(d_input, seg_num, seg_len, k, d_output_values, d_output_indices,
-                        d_workspace, workspace_bytes, stream, true);
+                        d_workspace, workspace_bytes, stream, bt::kBF16);
 }
 
 size_t bt_topk_bf16_segmented_workspace_size(int seg_num, long long max_total_len, int k) {
@@ -399,7 +436,29 @@ int bt_topk_bf16_segmented(const void* d_input, const int* d_offsets, int seg_nu
                            int* d_output_indices, void* d_workspace, size_t workspace_bytes,
                            void* stream) {
   return bt::topk_csr(d_input, d_offsets, seg_num, max_total_len, k, d_output_values,
-                      d_output_indices, d_workspace, workspace_bytes, stream, true);
+                      d_output_indices, d_workspace, workspace_bytes, stream, bt::kBF16);
+}
+
+size_t bt_topk_f32_workspace_size(int seg_num, int seg_len, int k) {
+  return bt::fixed_workspace(seg_num, seg_len, k, bt::kF32);
+}
+
+int bt_topk_f32(const void* d_input, int seg_num, int seg_len, int k, void* d_output_values,
+                int* d_output_indices, void* d_workspace, size_t workspace_bytes, void* stream) {
+  return bt::topk_fixed(d_input, seg_num, seg_len, k, d_output_values, d_output_indices,
+                        d_workspace, workspace_bytes, stream, bt::kF32);
+}
+
+size_t bt_topk_f32_segmented_workspace_size(int seg_num, long long max_total_len, int k) {
+  return bt::csr_workspace(seg_num, max_total_len, k, bt::kF32);
+}
+
+int bt_topk_f32_segmented(const void* d_input, const int* d_offsets, int seg_num,
+                          long long max_total_len, int k, void* d_output_values,
+                          int* d_output_indices, void* d_workspace, size_t workspace_bytes,
+                          void* stream) {
+  return bt::topk_csr(d_input, d_offsets, seg_num, max_total_len, k, d_output_values,
+                      d_output_indices, d_workspace, workspace_bytes, stream, bt::kF32);
 }
 
 int bt_workspace_status(const void* d_workspace, int seg_num, void* stream, unsigned* stats) {

@@ -42,6 +42,7 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "bt_common.cuh"
 #include "bt_device.cuh"
 
 namespace bt {
@@ -74,13 +75,16 @@ struct TopkParams {
   uint16_t* out_values;          // [seg_num * k]
   int* out_indices;              // [seg_num * k]
   uint32_t pad_bits;             // -inf of the element type: the value of a missing entry
+  int epv_shift;                 // log2 of the elements in a 16-byte vector: 3 (16-bit), 2 (fp32)
+  uint32_t* out_values32;        // [seg_num * k] value bits of 32-bit elements (fp32 entry points)
   uint32_t handoff_tries;        // tries of each consumer <-> merger hand-off wait (kWaitCap;
                                  // fewer only through the failure-path test hook)
   long long max_total_len;       // CSR: the caller's bound on offsets[seg_num] - offsets[0]
 };
 
 struct SegGeom {
-  long long a0, a1;  // aligned element coordinates of the segment [start, end)
+  long long a0, a1;  // aligned element coordinates of the segment [start, end) (elements of the
+                     // input's own type, counted from the 16-byte boundary below the input)
   long long v0;      // first aligned 16-byte vector
   long long nv;      // vectors spanned
   int nchunks;
@@ -100,8 +104,9 @@ __device__ __forceinline__ SegGeom seg_geom(const TopkParams& p, int s) {
   SegGeom g;
   g.a0 = g0 + p.shift;
   g.a1 = g1 + p.shift;
-  g.v0 = g.a0 >> 3;
-  g.nv = (g.a1 > g.a0) ? ((g.a1 + 7) >> 3) - g.v0 : 0;
+  const int sh = p.epv_shift;
+  g.v0 = g.a0 >> sh;
+  g.nv = (g.a1 > g.a0) ? ((g.a1 + (1 << sh) - 1) >> sh) - g.v0 : 0;
   g.nchunks = static_cast<int>((g.nv + kVecPerChunk - 1) / kVecPerChunk);
   g.chunk_vecs = g.nchunks ? static_cast<int>((g.nv + g.nchunks - 1) / g.nchunks) : 0;
   return g;
@@ -301,9 +306,10 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
     const long long rem = g.v0 + g.nv - si.cv0;
     si.nvc = static_cast<int>(rem < g.chunk_vecs ? rem : g.chunk_vecs);
     const long long first = g.v0 - si.cv0;
-    const long long last = ((g.a1 - 1) >> 3) - si.cv0;
-    si.vlo = ((g.a0 & 7) && first >= 0 && first < si.nvc) ? static_cast<int>(first) : -1;
-    si.vhi = ((g.a1 & 7) && last >= 0 && last < si.nvc) ? static_cast<int>(last) : -1;
+    const long long emask = (1ll << p.epv_shift) - 1;  // element position within a vector
+    const long long last = ((g.a1 - 1) >> p.epv_shift) - si.cv0;
+    si.vlo = ((g.a0 & emask) && first >= 0 && first < si.nvc) ? static_cast<int>(first) : -1;
+    si.vhi = ((g.a1 & emask) && last >= 0 && last < si.nvc) ? static_cast<int>(last) : -1;
     return si;
   };
   if (p.steal) {
@@ -545,8 +551,10 @@ __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
       }
       if (nch == 0) {
         for (int r = 0; r < p.k; ++r) {
-          p.out_values[static_cast<long long>(s) * p.k + r] = static_cast<uint16_t>(p.pad_bits);
-          p.out_indices[static_cast<long long>(s) * p.k + r] = -1;
+          const long long o = static_cast<long long>(s) * p.k + r;
+          if (p.out_values32) p.out_values32[o] = p.pad_bits;
+          else p.out_values[o] = static_cast<uint16_t>(p.pad_bits);
+          p.out_indices[o] = -1;
         }
       }
     }
@@ -583,3 +591,6 @@ __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
 #include "bt_body.cuh"
 #undef BT_ELEM_BF16
 #undef BT_ELEM_NS
+
+// 32-bit floats: a separate consumer on the same producer, set-up kernels and workspace layout.
+#include "bt_f32.cuh"

@@ -48,54 +48,6 @@ struct SCount {
   bool fail;
 };
 
-// 16-bit field j of four packed words (selects rather than indexing, so a run-time j keeps
-// the words in registers).
-__device__ __forceinline__ uint32_t field16(const uint32_t (&w)[4], int j) {
-  const uint32_t x = j < 2 ? w[0] : (j < 4 ? w[1] : (j < 6 ? w[2] : w[3]));
-  return (x >> ((j & 1) * 16)) & 0xFFFFu;
-}
-
-// Inclusive warp scan of four words of packed 16-bit counts.
-__device__ __forceinline__ void warp_scan4(uint32_t (&w)[4]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, w[i], o);
-      if (lane >= o) w[i] += y;
-    }
-  }
-}
-
-// Per-round block offsets from the warps' inclusive round totals in rw[w][half * 4 ...]:
-// base_j = (survivors of rounds before j) + (round j survivors of lower warps) + (round j
-// survivors of lower lanes).  Returns the grand total.
-__device__ __forceinline__ uint32_t round_bases(const uint32_t (*rw)[8], int half,
-                                                const uint32_t (&incl)[4],
-                                                const uint32_t (&own)[4], uint32_t (&base)[4]) {
-  const int warp = threadIdx.x >> 5;
-  uint32_t tot[4] = {0, 0, 0, 0}, pre[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    const uint4 v = lds128(&rw[w][half * 4]);
-    const uint32_t x[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      tot[i] += x[i];
-      pre[i] += w < warp ? x[i] : 0u;
-    }
-  }
-  uint32_t start = 0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint32_t b = start + field16(pre, j) + field16(incl, j) - field16(own, j);
-    if (j & 1) base[j >> 1] |= b << 16; else base[j >> 1] = b;
-    start += field16(tot, j);
-  }
-  return start;
-}
-
 // Counts the chunk's survivors under threshold T: key < T (STRICT), key <= T, or every value
 // (take_all, T == kNoThreshold).  TIES (non-strict, not take-all): survivors with key == T are
 // counted apart, so the caller can keep only the first ones by index.  One barrier.

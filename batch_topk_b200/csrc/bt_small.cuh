@@ -323,58 +323,6 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
 
 constexpr unsigned long long kEmpty = ~0ull;  // never a composite (indices are < 2^32 - 1)
 
-__device__ __forceinline__ unsigned long long shfl64(unsigned long long v, int src) {
-  const uint32_t lo = __shfl_sync(0xFFFFFFFFu, static_cast<uint32_t>(v), src);
-  const uint32_t hi = __shfl_sync(0xFFFFFFFFu, static_cast<uint32_t>(v >> 32), src);
-  return (static_cast<unsigned long long>(hi) << 32) | lo;
-}
-
-__device__ __forceinline__ unsigned long long shfl_xor64(unsigned long long v, int mask) {
-  const uint32_t lo = __shfl_xor_sync(0xFFFFFFFFu, static_cast<uint32_t>(v), mask);
-  const uint32_t hi = __shfl_xor_sync(0xFFFFFFFFu, static_cast<uint32_t>(v >> 32), mask);
-  return (static_cast<unsigned long long>(hi) << 32) | lo;
-}
-
-// One bitonic compare-exchange step (block `size`, distance `stride`) over the striped array;
-// size == 0 means "ascending everywhere" (the final merge of a bitonic sequence).
-template <int R>
-__device__ __forceinline__ void bitonic_step(unsigned long long (&x)[R], int size, int stride) {
-  const int lane = threadIdx.x & 31;
-  if (stride >= 32) {
-    const int rs = stride >> 5;
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if ((r & rs) == 0) {
-        const bool up = size == 0 || (((r << 5) + lane) & size) == 0;
-        const unsigned long long a = x[r], b = x[r | rs];
-        if ((a > b) == up) {
-          x[r] = b;
-          x[r | rs] = a;
-        }
-      }
-    }
-  } else {
-    const bool lower = (lane & stride) == 0;
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const bool up = size == 0 || (((r << 5) + lane) & size) == 0;
-      const unsigned long long y = shfl_xor64(x[r], stride);
-      const unsigned long long mn = x[r] < y ? x[r] : y;
-      const unsigned long long mx = x[r] < y ? y : x[r];
-      x[r] = (lower == up) ? mn : mx;
-    }
-  }
-}
-
-template <int R>
-__device__ __forceinline__ void warp_sort_regs(unsigned long long (&x)[R]) {
-#pragma unroll
-  for (int size = 2; size <= 32 * R; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) bitonic_step<R>(x, size, stride);
-  }
-}
-
 // L <- the N smallest of L and B, both ascending.
 template <int R>
 __device__ __forceinline__ void merge_sorted(unsigned long long (&L)[R], const unsigned long long (&B)[R]) {

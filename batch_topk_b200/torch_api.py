@@ -1,7 +1,7 @@
 """Tensor-level helpers over the C ABI (PyTorch provides device memory and streams only).
 
-    values, indices = topk(x, k)                      # x: [seg_num, seg_len] fp16/bf16 on CUDA
-    values, indices = topk_segmented(x, offsets, k)   # x: 1-D fp16/bf16, offsets: int32 [seg_num+1]
+    values, indices = topk(x, k)                      # x: [seg_num, seg_len] fp16/bf16/fp32 on CUDA
+    values, indices = topk_segmented(x, offsets, k)   # x: 1-D fp16/bf16/fp32, offsets: int32 [seg_num+1]
 
 Values come back in x's dtype (the input's own bit patterns), indices as int32, both
 [seg_num, k]; descending by value, lower index first among equal values, NaN last.
@@ -17,6 +17,10 @@ from . import (
     batch_topk_bf16_segmented,
     batch_topk_bf16_segmented_workspace_size,
     batch_topk_bf16_workspace_size,
+    batch_topk_f32,
+    batch_topk_f32_segmented,
+    batch_topk_f32_segmented_workspace_size,
+    batch_topk_f32_workspace_size,
     batch_topk_half,
     batch_topk_half_segmented,
     batch_topk_half_segmented_workspace_size,
@@ -30,6 +34,8 @@ _ENTRY = {
                     batch_topk_half_segmented_workspace_size),
     torch.bfloat16: (batch_topk_bf16, batch_topk_bf16_workspace_size, batch_topk_bf16_segmented,
                      batch_topk_bf16_segmented_workspace_size),
+    torch.float32: (batch_topk_f32, batch_topk_f32_workspace_size, batch_topk_f32_segmented,
+                    batch_topk_f32_segmented_workspace_size),
 }
 
 
@@ -81,7 +87,7 @@ def topk(x: torch.Tensor, k: int, *, workspace: Workspace | None = None, stream=
     of x's device).  The workspace and the outputs are allocated on that stream.  With
     check=True the call waits for the result and raises if a device-side check failed."""
     if x.dtype not in _ENTRY or x.dim() != 2 or not x.is_cuda:
-        raise ValueError("x must be a 2-D float16 or bfloat16 CUDA tensor")
+        raise ValueError("x must be a 2-D float16, bfloat16 or float32 CUDA tensor")
     run, size, _, _ = _ENTRY[x.dtype]
     seg_num, seg_len = x.shape
     nbytes = size(seg_num, seg_len, k)
@@ -114,7 +120,7 @@ def topk_segmented(x: torch.Tensor, offsets: torch.Tensor, k: int, *,
     """CSR top-k (segment s = x[offsets[s]:offsets[s+1]]), with topk's device, stream and
     check semantics."""
     if x.dtype not in _ENTRY or x.dim() != 1 or not x.is_cuda:
-        raise ValueError("x must be a 1-D float16 or bfloat16 CUDA tensor")
+        raise ValueError("x must be a 1-D float16, bfloat16 or float32 CUDA tensor")
     _, _, run, size = _ENTRY[x.dtype]
     if offsets.dtype != torch.int32 or offsets.dim() != 1 or offsets.device != x.device:
         raise ValueError("offsets must be a 1-D int32 tensor on x's device")
@@ -194,7 +200,7 @@ def _topk_op(x: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
 @_topk_op.register_fake
 def _topk_op_fake(x: torch.Tensor, k: int):
     if x.dim() != 2 or x.dtype not in _ENTRY:
-        raise ValueError("x must be a 2-D float16 or bfloat16 tensor")
+        raise ValueError("x must be a 2-D float16, bfloat16 or float32 tensor")
     return (x.new_empty((x.shape[0], k)), x.new_empty((x.shape[0], k), dtype=torch.int32))
 
 

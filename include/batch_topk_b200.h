@@ -76,6 +76,25 @@ int bt_topk_bf16_segmented(const void* d_input, const int* d_offsets, int seg_nu
 
 size_t bt_topk_bf16_segmented_workspace_size(int seg_num, long long max_total_len, int k);
 
+/* float32 inputs; no reference counterpart (the reference is fp16 only and lists other types as
+ * a non-goal).  The same arguments, layouts, limits, error contract and order as the fp16 entry
+ * points, with float32 values and values out: d_input and d_output_values hold 32-bit bit
+ * patterns and must be 4-byte aligned.  Order: descending, equal values (-0 == +0) by lower
+ * index, every NaN last.  Output values are the input's own bit patterns; a missing entry of a
+ * short CSR segment is -inf (0xFF800000) with index -1.  The workspace sizes are these
+ * functions' own (a 16-byte vector holds 4 values here, not 8). */
+int bt_topk_f32(const void* d_input, int seg_num, int seg_len, int k, void* d_output_values,
+                int* d_output_indices, void* d_workspace, size_t workspace_bytes, void* stream);
+
+size_t bt_topk_f32_workspace_size(int seg_num, int seg_len, int k);
+
+int bt_topk_f32_segmented(const void* d_input, const int* d_offsets, int seg_num,
+                          long long max_total_len, int k, void* d_output_values,
+                          int* d_output_indices, void* d_workspace, size_t workspace_bytes,
+                          void* stream);
+
+size_t bt_topk_f32_segmented_workspace_size(int seg_num, long long max_total_len, int k);
+
 /* bt_topk_half without a caller workspace; NO COUNTERPART IN THE REFERENCE, which always takes
  * a caller-allocated workspace (include/batch_topk.cuh:10-19).
  *

@@ -72,6 +72,13 @@ class Oracle:
         lib.oracle_topk_batch_bf16.restype = C.c_int
         lib.oracle_topk_csr_bf16.argtypes = lib.oracle_topk_csr.argtypes
         lib.oracle_topk_csr_bf16.restype = C.c_int
+        u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+        lib.oracle_topk_batch_f32.argtypes = [u32p, C.c_int64, C.c_int64, C.c_int, u32p, i32p, C.c_int, C.c_int]
+        lib.oracle_topk_batch_f32.restype = C.c_int
+        lib.oracle_topk_csr_f32.argtypes = [u32p, i64p, C.c_int64, C.c_int, u32p, i32p, C.c_int, C.c_int]
+        lib.oracle_topk_csr_f32.restype = C.c_int
+        lib.oracle_encode_desc_f32.argtypes = [C.c_uint32]
+        lib.oracle_encode_desc_f32.restype = C.c_uint32
         lib.oracle_encode_desc_bf16.argtypes = [C.c_uint16]
         lib.oracle_encode_desc_bf16.restype = C.c_uint16
         lib.oracle_bf16_to_float.argtypes = [C.c_uint16]
@@ -113,6 +120,33 @@ class Oracle:
                 threads or os.cpu_count() or 1)
         if rc != 0:
             raise ValueError("oracle_topk_csr rejected the arguments")
+        return ov, oi
+
+    def topk_f32(self, values_bits: np.ndarray, k: int, method: int = METHOD_COUNT,
+                 threads: int | None = None):
+        """Top-k of each row of a 2-D array of float32 bit patterns (uint32)."""
+        x = np.ascontiguousarray(values_bits).view(np.uint32)
+        assert x.ndim == 2
+        seg_num, seg_len = x.shape
+        ov = np.empty((seg_num, k), np.uint32)
+        oi = np.empty((seg_num, k), np.int32)
+        rc = self.lib.oracle_topk_batch_f32(x.reshape(-1), seg_num, seg_len, k, ov.reshape(-1),
+                                            oi.reshape(-1), method, threads or os.cpu_count() or 1)
+        if rc != 0:
+            raise ValueError("oracle_topk_batch_f32 rejected the arguments")
+        return ov, oi
+
+    def topk_csr_f32(self, values_bits: np.ndarray, offsets: np.ndarray, k: int,
+                     method: int = METHOD_COUNT, threads: int | None = None):
+        x = np.ascontiguousarray(values_bits).view(np.uint32).reshape(-1)
+        off = np.ascontiguousarray(offsets, dtype=np.int64)
+        seg_num = off.shape[0] - 1
+        ov = np.empty((seg_num, k), np.uint32)
+        oi = np.empty((seg_num, k), np.int32)
+        rc = self.lib.oracle_topk_csr_f32(x, off, seg_num, k, ov.reshape(-1), oi.reshape(-1),
+                                          method, threads or os.cpu_count() or 1)
+        if rc != 0:
+            raise ValueError("oracle_topk_csr_f32 rejected the arguments")
         return ov, oi
 
     def histogram_pass(self, values_bits, shift, prefix, prefix_mask):

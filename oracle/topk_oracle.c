@@ -31,6 +31,11 @@
  * a listed non-goal), so this restates the same comparator on bfloat16 values converted
  * exactly to float, and the same descending key with bfloat16's NaN test (exponent field
  * 0x7F80); padding is bfloat16 -inf, 0xFF80.
+ *
+ * float32 rows (the *_f32 drivers, 32-bit bit patterns): likewise no reference path; the same
+ * comparator on the float values themselves, and for the count method a 32-bit descending key
+ * (any NaN -> 0xFFFFFFFF, +-0 -> 0x7FFFFFFF, else bits ^ (sign ? 0 : 0x7FFFFFFF)) selected with
+ * four 8-bit counting passes; padding is float32 -inf, 0xFF800000.
  */
 #include <math.h>
 #include <pthread.h>
@@ -291,6 +296,146 @@ int oracle_topk_batch_bf16(const uint16_t* in, int64_t seg_num, int64_t seg_len,
 int oracle_topk_csr_bf16(const uint16_t* in, const int64_t* offsets, int64_t seg_num, int k,
                          uint16_t* out_v, int32_t* out_i, int method, int threads) {
   return run_batch(in, offsets, seg_num, 0, k, out_v, out_i, method, threads, 1);
+}
+
+/* ---- float32 rows ------------------------------------------------------------------ */
+
+uint32_t oracle_encode_desc_f32(uint32_t bits) {
+  if ((bits & 0x7fffffffu) > 0x7f800000u) return 0xffffffffu; /* any NaN */
+  if ((bits & 0x7fffffffu) == 0) return 0x7fffffffu;          /* +-0 */
+  return (bits & 0x80000000u) ? bits : (bits ^ 0x7fffffffu);
+}
+
+static int topk_sort_segment_f32(const uint32_t* in, int len, int k, uint32_t* out_v,
+                                 int32_t* out_i) {
+  if (len <= 0 || k <= 0) return 0;
+  float* v = (float*)malloc(sizeof(float) * (size_t)len);
+  int* idx = (int*)malloc(sizeof(int) * (size_t)len);
+  int* tmp = (int*)malloc(sizeof(int) * (size_t)len);
+  memcpy(v, in, sizeof(float) * (size_t)len);
+  for (int i = 0; i < len; ++i) idx[i] = i;
+  merge_sort_idx(v, idx, tmp, len);
+  const int kk = k < len ? k : len;
+  for (int r = 0; r < kk; ++r) {
+    out_i[r] = idx[r];
+    out_v[r] = in[idx[r]];
+  }
+  free(v);
+  free(idx);
+  free(tmp);
+  return kk;
+}
+
+static int topk_count_segment_f32(const uint32_t* in, int len, int k, uint32_t* out_v,
+                                  int32_t* out_i) {
+  if (len <= 0 || k <= 0) return 0;
+  const int kk = k < len ? k : len;
+  uint32_t h[256];
+  uint32_t prefix = 0, cum = 0;
+  for (int d = 3; d >= 0; --d) { /* most significant digit first */
+    memset(h, 0, sizeof(h));
+    const int sh = 8 * d;
+    for (int i = 0; i < len; ++i) {
+      const uint32_t key = oracle_encode_desc_f32(in[i]);
+      if (d == 3 || (key >> (sh + 8)) == (prefix >> (sh + 8))) ++h[(key >> sh) & 0xffu];
+    }
+    int b = 0;
+    for (; b < 256; ++b) {
+      if (cum + h[b] >= (uint32_t)kk) break;
+      cum += h[b];
+    }
+    prefix |= (uint32_t)b << sh;
+  }
+  const uint32_t cutoff = prefix;
+  int need = kk - (int)cum; /* ties at the cutoff that make it, lowest index first */
+  uint64_t* sel = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)kk);
+  int n = 0;
+  for (int i = 0; i < len; ++i) {
+    const uint32_t key = oracle_encode_desc_f32(in[i]);
+    if (key < cutoff || (key == cutoff && need > 0)) {
+      if (key == cutoff) --need;
+      sel[n++] = ((uint64_t)key << 32) | (uint32_t)i;
+    }
+  }
+  qsort(sel, (size_t)n, sizeof(uint64_t), cmp_key_idx);
+  for (int r = 0; r < n; ++r) {
+    const int i = (int)(uint32_t)sel[r];
+    out_i[r] = i;
+    out_v[r] = in[i];
+  }
+  free(sel);
+  return n;
+}
+
+typedef struct {
+  const uint32_t* in;
+  const int64_t* offsets;
+  int64_t seg_len;
+  int k;
+  int method;
+  uint32_t* out_v;
+  int32_t* out_i;
+  int64_t seg_begin, seg_end;
+} job32_t;
+
+static void* run_job_f32(void* arg) {
+  job32_t* j = (job32_t*)arg;
+  for (int64_t s = j->seg_begin; s < j->seg_end; ++s) {
+    int64_t start, len;
+    if (j->offsets) {
+      start = j->offsets[s];
+      len = j->offsets[s + 1] - j->offsets[s];
+    } else {
+      start = s * j->seg_len;
+      len = j->seg_len;
+    }
+    uint32_t* ov = j->out_v + s * (int64_t)j->k;
+    int32_t* oi = j->out_i + s * (int64_t)j->k;
+    const int n = j->method == 0 ? topk_sort_segment_f32(j->in + start, (int)len, j->k, ov, oi)
+                                 : topk_count_segment_f32(j->in + start, (int)len, j->k, ov, oi);
+    for (int r = n; r < j->k; ++r) {
+      ov[r] = 0xff800000u;
+      oi[r] = -1;
+    }
+  }
+  return NULL;
+}
+
+static int run_batch_f32(const uint32_t* in, const int64_t* offsets, int64_t seg_num,
+                         int64_t seg_len, int k, uint32_t* out_v, int32_t* out_i, int method,
+                         int threads) {
+  if (seg_num <= 0 || k <= 0) return -1;
+  if (threads < 1) threads = 1;
+  if (threads > seg_num) threads = (int)seg_num;
+  pthread_t* tid = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)threads);
+  job32_t* jobs = (job32_t*)malloc(sizeof(job32_t) * (size_t)threads);
+  for (int t = 0; t < threads; ++t) {
+    jobs[t].in = in;
+    jobs[t].offsets = offsets;
+    jobs[t].seg_len = seg_len;
+    jobs[t].k = k;
+    jobs[t].method = method;
+    jobs[t].out_v = out_v;
+    jobs[t].out_i = out_i;
+    jobs[t].seg_begin = seg_num * t / threads;
+    jobs[t].seg_end = seg_num * (t + 1) / threads;
+    pthread_create(&tid[t], NULL, run_job_f32, &jobs[t]);
+  }
+  for (int t = 0; t < threads; ++t) pthread_join(tid[t], NULL);
+  free(tid);
+  free(jobs);
+  return 0;
+}
+
+int oracle_topk_batch_f32(const uint32_t* in, int64_t seg_num, int64_t seg_len, int k,
+                          uint32_t* out_v, int32_t* out_i, int method, int threads) {
+  if (seg_len <= 0) return -1;
+  return run_batch_f32(in, NULL, seg_num, seg_len, k, out_v, out_i, method, threads);
+}
+
+int oracle_topk_csr_f32(const uint32_t* in, const int64_t* offsets, int64_t seg_num, int k,
+                        uint32_t* out_v, int32_t* out_i, int method, int threads) {
+  return run_batch_f32(in, offsets, seg_num, 0, k, out_v, out_i, method, threads);
 }
 
 /* ---- select-state restatements, for the reference's known-answer tests ----------- */

@@ -30,7 +30,7 @@ def test_fake_kernel_rejects_wrong_dtype():
     from torch._subclasses.fake_tensor import FakeTensorMode
 
     with FakeTensorMode(), pytest.raises(ValueError):
-        torch.ops.batch_topk_b200.topk(torch.empty((2, 10), dtype=torch.float32, device="cuda"), 3)
+        torch.ops.batch_topk_b200.topk(torch.empty((2, 10), dtype=torch.float64, device="cuda"), 3)
 
 
 def test_fake_kernels_keep_bfloat16():
@@ -46,13 +46,22 @@ def test_fake_kernels_keep_bfloat16():
         assert v.shape == (3, 5) and v.dtype == torch.bfloat16
 
 
+def test_fake_kernels_keep_float32():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        x = torch.empty((3, 500), dtype=torch.float32, device="cuda")
+        v, i = torch.ops.batch_topk_b200.topk(x, 7)
+        assert v.shape == (3, 7) and v.dtype == torch.float32 and i.dtype == torch.int32
+
+
 def test_eager_calls_reject_host_tensors_and_other_dtypes():
     from batch_topk_b200 import torch_api
 
     with pytest.raises(ValueError):
         torch_api.topk(torch.zeros((2, 10), dtype=torch.float16), 3)       # host memory
     with pytest.raises(ValueError):
-        torch_api.topk(torch.zeros((2, 10), dtype=torch.float32), 3)       # not 16-bit
+        torch_api.topk(torch.zeros((2, 10), dtype=torch.float64), 3)       # no float64 path
     with pytest.raises(ValueError):
         torch_api.topk_segmented(torch.zeros((10,), dtype=torch.bfloat16),
                                  torch.zeros((3,), dtype=torch.int32), 2)

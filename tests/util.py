@@ -110,3 +110,26 @@ def expected_from_indices(bits_rows, idx):
         m = idx[r] >= 0
         out[r, m] = row[idx[r, m]]
     return out
+
+
+def _dev_copy32(torch, bits: np.ndarray, misalign: int, device):
+    """32-bit patterns on the device, starting `misalign` floats past a 16-byte boundary."""
+    flat = np.ascontiguousarray(bits, dtype=np.uint32).reshape(-1)
+    buf = torch.empty(flat.size + 8, dtype=torch.int32, device=device)
+    buf.fill_(0x5A5A5A5A)  # junk around the payload must never leak into results
+    view = buf[misalign : misalign + flat.size]
+    view.copy_(torch.from_numpy(flat.view(np.int32)))
+    return buf, view
+
+
+def assert_exact32(got_v, got_i, exp_v, exp_i, what=""):
+    """Bit-exact compare of 32-bit value patterns and int32 indices."""
+    got_v = np.asarray(got_v, np.uint32)
+    exp_v = np.asarray(exp_v, np.uint32)
+    bad = (got_i != exp_i) | (got_v != exp_v)
+    if bad.any():
+        r, c = np.argwhere(bad)[0]
+        raise AssertionError(
+            f"{what}: {int(bad.sum())} mismatches; first at row {r} rank {c}: got "
+            f"(idx {got_i[r, c]}, 0x{int(got_v[r, c]):08x}) expected (idx {exp_i[r, c]}, "
+            f"0x{int(exp_v[r, c]):08x})")
