@@ -50,6 +50,16 @@ __device__ __forceinline__ uint32_t word_of(const uint4& w, int e) {
   return e == 0 ? w.x : (e == 1 ? w.y : (e == 2 ? w.z : w.w));
 }
 
+// The float whose key is `key` (+0 for the key of zero).  Keys of numbers run from 0x007FFFFF
+// (+inf) to 0xFF800000 (-inf); above that (bucket bounds, the NaN key) the bits are a NaN.
+__device__ __forceinline__ float key_value(uint32_t key) {
+  return __uint_as_float(key < 0x80000000u ? (key ^ 0x7FFFFFFFu) : key);
+}
+
+// Is `key < T` the float compare `value > key_value(T)` (false for a NaN value)?  Yes while T
+// is the key of a number.
+__device__ __forceinline__ bool float_threshold(uint32_t T) { return T <= 0xFF800000u; }
+
 __device__ __forceinline__ unsigned long long comp(uint32_t key, uint32_t idx) {
   return (static_cast<unsigned long long>(key) << 32) | idx;
 }
@@ -102,13 +112,18 @@ struct FState {
 // slot i holds a key), by four 8-bit digit passes, most significant first.  Returns it and,
 // in *before, how many keys are smaller; when fewer than k keys exist, returns false.
 // The histogram is zero on entry and left zero.
-template <int N, class KeyFn>
+//
+// With PASSES = 2 only the top 16 bits are resolved: the result is then the largest key of the
+// 65536-key bucket that holds the k-th key (at least k keys are <= it, and no key of a lower
+// bucket reaches it), a certified bound at half the cost, loose by at most that bucket (a
+// relative 2^-7 of the value for normal floats).
+template <int N, int PASSES = 4, class KeyFn>
 __device__ __forceinline__ bool block_kth32(KeyFn&& key, uint32_t k, FScratch& sm,
                                             uint32_t* kth, uint32_t* before) {
   const int tid = threadIdx.x;
   uint32_t prefix = 0, base = 0;
 #pragma unroll 1
-  for (int d = 3; d >= 0; --d) {
+  for (int d = 3; d >= 4 - PASSES; --d) {
     const int sh = 8 * d;
 #pragma unroll
     for (int i = 0; i < N; ++i) {
@@ -130,7 +145,7 @@ __device__ __forceinline__ bool block_kth32(KeyFn&& key, uint32_t k, FScratch& s
     base = bf;
     prefix |= static_cast<uint32_t>(b) << sh;
   }
-  *kth = prefix;
+  *kth = PASSES == 4 ? prefix : (prefix | 0xFFFFu);
   *before = base;
   return true;
 }
@@ -161,6 +176,9 @@ __device__ __forceinline__ FCount fcount(const StageInfo& si, const uint8_t* buf
   FCount c;
   c.M = 0;
   c.E = 0;
+  // a strict threshold below the NaN key is a float compare against its value
+  const bool fcmp = MODE == kLt && float_threshold(T);
+  const float V = key_value(T);
   uint32_t own[4] = {0, 0, 0, 0}, owne[4] = {0, 0, 0, 0};
 #pragma unroll
   for (int j = 0; j < kVecPerThread; ++j) {
@@ -170,11 +188,16 @@ __device__ __forceinline__ FCount fcount(const StageInfo& si, const uint8_t* buf
       uint32_t m = 0, e = 0;
 #pragma unroll
       for (int x = 0; x < 4; ++x) {
-        const uint32_t key = desc_key32(word_of(w, x));
-        const bool lt = key < T, eq = key == T;
-        const bool pass = MODE == kAll ? true : (MODE == kLt ? lt : (lt || eq));
+        bool pass;
+        if (MODE == kLt && fcmp) {  // key < T  <=>  value > V (false for a NaN value)
+          pass = __uint_as_float(word_of(w, x)) > V;
+        } else {
+          const uint32_t key = desc_key32(word_of(w, x));
+          const bool lt = key < T, eq = key == T;
+          pass = MODE == kAll ? true : (MODE == kLt ? lt : (lt || eq));
+          if (MODE == kTies) e |= static_cast<uint32_t>(eq) << x;
+        }
         m |= static_cast<uint32_t>(pass) << x;
-        if (MODE == kTies) e |= static_cast<uint32_t>(eq) << x;
       }
       if (vi == si.vlo || vi == si.vhi) {
         const uint32_t vm = valid_mask4(si.cv0 + vi, si.a0, si.a1);
@@ -245,6 +268,97 @@ __device__ __forceinline__ void fappend(const StageInfo& si, const uint8_t* buf,
   csync();
 }
 
+// ---- contiguous count and append (the steady state) ------------------------------------
+//
+// Thread t owns vectors 8t .. 8t+7 (visited rotated by t mod 8, so a quarter-warp's 16-byte
+// loads cover all banks): one warp scan and one barrier give each thread its first output
+// position, and each thread writes its own survivors.  Cheapest while survivors are few and
+// spread; when one thread holds many, the strided form spreads the writes instead.
+struct CCount32 {
+  uint32_t M;  // survivors: bit 4 j + e = element e of the thread's vector 8t + j
+  uint32_t base, total, maxcnt;
+  bool fail;
+};
+
+// STRICT: key < K (value > V); otherwise key <= K (value >= V).  K is the key of a number.
+template <bool STRICT>
+__device__ __forceinline__ CCount32 fcount_contig(const StageInfo& si, const uint8_t* buf,
+                                                  FScratch& sm, uint32_t K, int& par) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const float V = key_value(K);
+  const int sw = tid & 7;
+  CCount32 c;
+  c.M = 0;
+#pragma unroll
+  for (int jj = 0; jj < kVecPerThread; ++jj) {
+    const int j = jj ^ sw;
+    const int vi = tid * kVecPerThread + j;
+    if (vi < si.nvc) {
+      const uint4 w = lds128(buf + vi * 16);
+      const float a = __uint_as_float(w.x), b = __uint_as_float(w.y),
+                  cc = __uint_as_float(w.z), d = __uint_as_float(w.w);
+      uint32_t m = STRICT ? ((a > V ? 1u : 0u) | (b > V ? 2u : 0u) | (cc > V ? 4u : 0u) |
+                             (d > V ? 8u : 0u))
+                          : ((a >= V ? 1u : 0u) | (b >= V ? 2u : 0u) | (cc >= V ? 4u : 0u) |
+                             (d >= V ? 8u : 0u));
+      if (vi == si.vlo || vi == si.vhi) m &= valid_mask4(si.cv0 + vi, si.a0, si.a1);
+      c.M |= m << (4 * j);
+    }
+  }
+  const uint32_t cnt = static_cast<uint32_t>(__popc(c.M));
+  uint32_t incl = 0, wmax = 0;
+  if (__ballot_sync(0xFFFFFFFFu, cnt != 0)) {
+    incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    wmax = __reduce_max_sync(0xFFFFFFFFu, cnt);
+  }
+  if (lane == 31) sm.rw[par][warp][0] = incl | (wmax << 16);  // total <= 8192, max <= 32
+  csync();
+  c.fail = sm.fail != 0;
+  uint32_t total = 0, wpre = 0, mx = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const uint32_t t = sm.rw[par][w][0];
+    wpre += w < warp ? (t & 0xFFFFu) : 0u;
+    total += t & 0xFFFFu;
+    mx = (t >> 16) > mx ? (t >> 16) : mx;
+  }
+  c.total = total;
+  c.maxcnt = mx;
+  c.base = wpre + incl - cnt;
+  par ^= 1;
+  return c;
+}
+
+__device__ __forceinline__ void fappend_contig(const StageInfo& si, const uint8_t* buf,
+                                               const CCount32& c, FScratch& sm, uint32_t nbuf) {
+  const int tid = threadIdx.x;
+  unsigned long long* out = sm.cache + nbuf + c.base;
+  uint32_t r = 0;
+#pragma unroll 1
+  for (int j = 0; j < kVecPerThread; ++j) {
+    uint32_t m = (c.M >> (4 * j)) & 0xFu;
+    if (m == 0) continue;
+    const int vi = tid * kVecPerThread + j;
+    const uint4 w = lds128(buf + vi * 16);
+    const long long e0 = (si.cv0 + vi) * 4 - si.a0;
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+      if ((m >> x) & 1u) out[r++] = comp(desc_key32(word_of(w, x)), static_cast<uint32_t>(e0 + x));
+    }
+  }
+  csync();
+}
+
+// A thread holding more survivors than this writes too long alone: the strided form is used.
+constexpr uint32_t kClusterMax = 16;
+
 // ---- cache maintenance -----------------------------------------------------------------
 
 // Keeps, in order, the cache entries with key < K and the first `need` with key == K; returns
@@ -302,7 +416,8 @@ __device__ void fcut_to_k(FScratch& sm, FState& fs, uint32_t k) {
   fs.added = 0;
 }
 
-// The cache's exact k-th key (it holds at least k), without cutting.
+// The cache's exact k-th key (it holds at least k), without cutting.  Exact, not a bucket
+// bound: on tie-heavy rows only the exact key as a strict threshold leaves later chunks quiet.
 __device__ uint32_t fcache_kth(FScratch& sm, uint32_t n, uint32_t k) {
   constexpr int kPer = kCache / kThreads;
   const uint32_t i0 = threadIdx.x * kPer;
@@ -319,9 +434,9 @@ __device__ uint32_t fcache_kth(FScratch& sm, uint32_t n, uint32_t k) {
 
 // ---- per-chunk thresholds --------------------------------------------------------------
 
-// The chunk's k-th best group maximum (8 groups of 4 floats per thread, 2048 in all: each
-// maximum is a distinct element, so at least k elements have key <= it).  False when fewer
-// than k groups hold a number.
+// A certified chunk threshold from the group maxima (8 groups of 4 floats per thread, 2048 in
+// all; each maximum is a distinct element): the 16-bit bucket bound of their k-th best key, so
+// at least k elements have a key <= it.  False when fewer than k groups hold a number.
 __device__ bool fgroup_kth(const StageInfo& si, const uint8_t* buf, FScratch& sm, uint32_t k,
                            uint32_t* kc) {
   const int tid = threadIdx.x;
@@ -351,7 +466,7 @@ __device__ bool fgroup_kth(const StageInfo& si, const uint8_t* buf, FScratch& sm
 #pragma unroll
   for (int g = 0; g < 8; ++g) keys[g] = desc_key32(__float_as_uint(mx[g]));
   uint32_t before;
-  return block_kth32<8>(
+  return block_kth32<8, 2>(
       [&](int i, uint32_t* v) {
         *v = keys[i];
         return keys[i] != kNaNKey;
@@ -406,32 +521,54 @@ __device__ bool fchunk(const StageInfo& si, const uint8_t* buf, FScratch& sm, FS
                        uint32_t k, int& par) {
   constexpr uint32_t C = kCache;
   const int tid = threadIdx.x;
-  if (fs.quiet && fs.hasK) {  // after a quiet chunk: one OR-barrier decides
-    bool any = false;
+  if (fs.quiet && fs.hasK && float_threshold(fs.K)) {  // after a quiet chunk: one OR-barrier
+    // the maximum of the thread's values (fmaxf skips NaN) against the threshold's value
+    float mx = __int_as_float(0x7FC00000);
 #pragma unroll
     for (int j = 0; j < kVecPerThread; ++j) {
       const int vi = j * kThreads + tid;
       if (vi < si.nvc) {
-        const uint4 w = lds128(buf + vi * 16);
-        uint32_t m = 0;
-#pragma unroll
-        for (int x = 0; x < 4; ++x) m |= static_cast<uint32_t>(desc_key32(word_of(w, x)) < fs.K) << x;
-        if (vi == si.vlo || vi == si.vhi) m &= valid_mask4(si.cv0 + vi, si.a0, si.a1);
-        any = any || m != 0;
+        uint4 w = lds128(buf + vi * 16);
+        if (vi == si.vlo || vi == si.vhi) {
+          const uint32_t vm = valid_mask4(si.cv0 + vi, si.a0, si.a1);
+          if (!(vm & 1u)) w.x = 0x7FC00000u;
+          if (!(vm & 2u)) w.y = 0x7FC00000u;
+          if (!(vm & 4u)) w.z = 0x7FC00000u;
+          if (!(vm & 8u)) w.w = 0x7FC00000u;
+        }
+        mx = fmaxf(fmaxf(mx, fmaxf(__uint_as_float(w.x), __uint_as_float(w.y))),
+                   fmaxf(__uint_as_float(w.z), __uint_as_float(w.w)));
       }
     }
-    if (!group_or<kThreads>(any || sm.fail != 0)) return true;
+    if (!group_or<kThreads>(mx > key_value(fs.K) || sm.fail != 0)) return true;
   }
   FCount c;
   bool counted = false;
   if (fs.hasK && !fs.rising) {
-    c = fcount<kLt>(si, buf, sm, fs.K, par);
-    if (c.fail) return false;
-    if (c.total <= C - fs.nbuf) {
-      fappend<false>(si, buf, c, 0u, sm, fs.nbuf);
-      fs.nbuf += c.total;
-      fs.added += c.total;
-      fs.quiet = c.total == 0;
+    uint32_t total;
+    if (float_threshold(fs.K)) {
+      const CCount32 cc = fcount_contig<true>(si, buf, sm, fs.K, par);
+      if (cc.fail) return false;
+      total = cc.total;
+      if (total <= C - fs.nbuf) {
+        if (cc.maxcnt <= kClusterMax) {
+          fappend_contig(si, buf, cc, sm, fs.nbuf);
+        } else {
+          c = fcount<kLt>(si, buf, sm, fs.K, par);
+          if (c.fail) return false;
+          fappend<false>(si, buf, c, 0u, sm, fs.nbuf);
+        }
+      }
+    } else {
+      c = fcount<kLt>(si, buf, sm, fs.K, par);
+      if (c.fail) return false;
+      total = c.total;
+      if (total <= C - fs.nbuf) fappend<false>(si, buf, c, 0u, sm, fs.nbuf);
+    }
+    if (total <= C - fs.nbuf) {
+      fs.nbuf += total;
+      fs.added += total;
+      fs.quiet = total == 0;
       if (fs.added >= k && fs.nbuf >= k) {  // k more since the last tightening
         const uint32_t kk = fcache_kth(sm, fs.nbuf, k);
         if (kk < fs.K) fs.K = kk;
@@ -446,6 +583,20 @@ __device__ bool fchunk(const StageInfo& si, const uint8_t* buf, FScratch& sm, FS
   if (sm.fail) return false;
   const bool own = have_kc && (!fs.hasK || kc < fs.K);
   fs.rising = (counted || fs.rising) && own;
+  if (own && float_threshold(kc) && kCache - fs.nbuf >= k + k / 8) {
+    // every value with key <= kc, when the cache has room for them (the usual first chunk)
+    const CCount32 cc = fcount_contig<false>(si, buf, sm, kc, par);
+    if (cc.fail) return false;
+    if (cc.total <= C - fs.nbuf && cc.maxcnt <= kClusterMax) {
+      fappend_contig(si, buf, cc, sm, fs.nbuf);
+      fs.nbuf += cc.total;
+      fs.added = 0;
+      fs.quiet = false;
+      fs.K = kc;  // certified: >= k values with key <= kc are in the cache now
+      fs.hasK = true;
+      return true;
+    }
+  }
   if (own) {
     FCount t = fcount<kTies>(si, buf, sm, kc, par);
     if (t.fail) return false;
@@ -483,8 +634,9 @@ __device__ bool fchunk(const StageInfo& si, const uint8_t* buf, FScratch& sm, FS
 
 // ---- row output ------------------------------------------------------------------------
 
-// Writes row s from the n <= k composites at sm.cache[0 .. n) in ascending composite order,
-// the value bits read back from the input by index; slots n .. k-1 get -inf and index -1.
+// Writes row s from the n <= 1024 composites at sm.cache[0 .. n): the first k in ascending
+// composite order, the value bits read back from the input by index; when n < k, slots
+// n .. k-1 get -inf and index -1.
 __device__ void fsort_emit(const TopkParams& p, FScratch& sm, uint32_t n, int s, long long a0,
                            long long len) {
   const int tid = threadIdx.x;
@@ -551,7 +703,8 @@ __device__ void fclose(const TopkParams& p, FState& fs, FScratch& sm) {
   const uint32_t k = static_cast<uint32_t>(p.k);
   const long long len = fs.a1 - fs.a0;
   if (fs.mycnt == fs.nchunks) {
-    if (fs.nbuf > k) fcut_to_k(sm, fs, k);
+    // the sort ranks up to 1024 entries and writes the first k: no cut below that
+    if (fs.nbuf > 1024) fcut_to_k(sm, fs, k);
     fsort_emit(p, sm, fs.nbuf, fs.s, fs.a0, len);
     return;
   }
@@ -593,7 +746,7 @@ __device__ void fclose(const TopkParams& p, FState& fs, FScratch& sm) {
     csync();
   }
   fs.nbuf = n;
-  if (fs.nbuf > k) fcut_to_k(sm, fs, k);
+  if (fs.nbuf > 1024) fcut_to_k(sm, fs, k);
   fsort_emit(p, sm, fs.nbuf, fs.s, fs.a0, len);
 }
 

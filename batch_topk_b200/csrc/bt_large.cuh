@@ -453,9 +453,9 @@ __device__ bool large_chunk(const TopkParams& p, const StageInfo& si, const uint
 
 // ---- row output ----------------------------------------------------------------------
 
-// Writes row s from the n <= k composites at sm.cache[0 .. n): in ascending composite order
-// (key, then index: the reference's order, include/batch_topk_types.cuh:50-92) as value bits
-// and indices; slots n .. k-1 get the padding (-inf, index -1).  Warp w sorts entries
+// Writes row s from the n <= 1024 composites at sm.cache[0 .. n): the first k in ascending
+// composite order (key, then index: the reference's order, include/batch_topk_types.cuh:50-92)
+// as value bits and indices; when n < k, slots n .. k-1 get the padding (-inf, index -1).  Warp w sorts entries
 // [128 w, 128 w + 128) in registers (bitonic, 4 a lane); then every entry's rank is its place
 // in its own run plus, per other run, a binary search for the entries below it, and it is
 // written straight to that slot of the row.
@@ -465,7 +465,7 @@ __device__ void sort_emit(const TopkParams& p, LargeScratch& sm, uint32_t n, int
   const int lane = tid & 31;
   const uint32_t warp = static_cast<uint32_t>(tid >> 5);
   const uint32_t k = static_cast<uint32_t>(p.k);
-  const uint32_t runs = (n + 127) / 128;  // <= 8 runs of 128 (n <= k <= 1024)
+  const uint32_t runs = (n + 127) / 128;  // <= 8 runs of 128 (n <= 1024)
   unsigned long long x[4];
   if (warp < runs) {
 #pragma unroll
@@ -531,7 +531,8 @@ __device__ void large_close(const TopkParams& p, LargeState& ls, LargeScratch& s
   const uint32_t k = static_cast<uint32_t>(p.k);
   const long long len = ls.a1 - ls.a0;
   if (ls.mycnt == ls.nchunks) {
-    if (ls.nbuf > k) cut_to_k(sm, ls, k);
+    // the sort ranks up to 1024 entries and writes the first k: no cut below that
+    if (ls.nbuf > 1024) cut_to_k(sm, ls, k);
     sort_emit(p, sm, ls.nbuf, ls.s, len);
     return;
   }
@@ -575,7 +576,7 @@ __device__ void large_close(const TopkParams& p, LargeState& ls, LargeScratch& s
     csync();  // tbase is rewritten by the next round
   }
   ls.nbuf = n;
-  if (ls.nbuf > k) cut_to_k(sm, ls, k);
+  if (ls.nbuf > 1024) cut_to_k(sm, ls, k);
   sort_emit(p, sm, ls.nbuf, ls.s, len);
 }
 
