@@ -1,13 +1,14 @@
 """Time the library on the five benchmark configurations (or one of them), one JSON line each.
 
     python -m batch_topk_b200.cases [--config C1|C2|C3|C4|C5|N01] [--k K] [--iters N] [--rows R]
-                                    [--dtype f16|bf16]
+                                    [--dtype f16|bf16|f32]
 
 Inputs are generated on the device (batch_topk_b200.gen).  Each line gives the median time of
 the streaming kernel alone (CUDA events recorded around it on its stream by the library's
 profiling hook) and of the whole call, and the effective input bandwidth against the
 measured HBM copy peak.  With --dtype bf16 each generated fp16 value is converted to the
-nearest bfloat16 and the bf16 entry points run.  The same command is the target of the ncu
+nearest bfloat16 and the bf16 entry points run; with --dtype f32 it is widened (exactly) to
+float32 and the fp32 entry points run (4 bytes a value).  The same command is the target of the ncu
 summaries under profiles/.
 """
 from __future__ import annotations
@@ -20,6 +21,8 @@ import numpy as np
 import torch
 
 from . import batch_topk_bf16, batch_topk_bf16_segmented, batch_topk_bf16_segmented_workspace_size
+from . import batch_topk_f32, batch_topk_f32_segmented, batch_topk_f32_segmented_workspace_size
+from . import batch_topk_f32_workspace_size
 from . import batch_topk_bf16_workspace_size, batch_topk_half, batch_topk_half_segmented
 from . import batch_topk_half_segmented_workspace_size, batch_topk_half_workspace_size
 from . import set_profile_events, workspace_status
@@ -59,12 +62,18 @@ def run(config: str, k: int | None, iters: int, rows: int | None, outputs: bool 
     """One JSON-ready line; with outputs=True also (input, offsets, values, indices) on the device."""
     x, off, k0, n = make(config, rows)
     bf16 = dtype == "bf16"
+    f32 = dtype == "f32"
+    esize = 4 if f32 else 2
     if bf16:
         x = x.view(torch.float16).to(torch.bfloat16).view(torch.int16)
+    if f32:
+        x = x.view(torch.float16).float().view(torch.int32)
     fixed, fixed_ws = (batch_topk_bf16, batch_topk_bf16_workspace_size) if bf16 else (
-        batch_topk_half, batch_topk_half_workspace_size)
+        (batch_topk_f32, batch_topk_f32_workspace_size) if f32 else
+        (batch_topk_half, batch_topk_half_workspace_size))
     csr, csr_ws = (batch_topk_bf16_segmented, batch_topk_bf16_segmented_workspace_size) if bf16 else (
-        batch_topk_half_segmented, batch_topk_half_segmented_workspace_size)
+        (batch_topk_f32_segmented, batch_topk_f32_segmented_workspace_size) if f32 else
+        (batch_topk_half_segmented, batch_topk_half_segmented_workspace_size))
     k = k or k0
     dev = x.device
     s = torch.cuda.current_stream(dev)
@@ -77,7 +86,7 @@ def run(config: str, k: int | None, iters: int, rows: int | None, outputs: bool 
         nbytes = csr_ws(n, total, k)
         d_off = torch.from_numpy(off.astype(np.int32)).to(dev)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    ov = torch.empty((n, k), dtype=torch.int16, device=dev)
+    ov = torch.empty((n, k), dtype=torch.int32 if f32 else torch.int16, device=dev)
     oi = torch.empty((n, k), dtype=torch.int32, device=dev)
 
     def call():
@@ -111,7 +120,7 @@ def run(config: str, k: int | None, iters: int, rows: int | None, outputs: bool 
         set_profile_events(None, None)
     flags, _ = workspace_status(ws.data_ptr(), n, s.cuda_stream)
     kt, wt = float(np.median(kern)), float(np.median(whole))
-    gbs = total * 2 / kt / 1e6
+    gbs = total * esize / kt / 1e6
     line = {"config": config, "dtype": dtype, "segments": n, "k": k, "values": total, "kernel_us": round(kt * 1e3, 2),
             "call_us": round(wt * 1e3, 2), "input_gbs": round(gbs, 1),
             "pct_hbm": round(gbs / hbm_peak(), 4), "status": flags}
@@ -124,7 +133,7 @@ def main():
     ap.add_argument("--k", type=int, action="append", help="k values (C4: default 1, 8, 50, 256)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--rows", type=int, help="first R segments only (C5 defaults to 384)")
-    ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16")
+    ap.add_argument("--dtype", choices=["f16", "bf16", "f32"], default="f16")
     a = ap.parse_args()
     for config in a.config or ["C1", "C2", "C3", "N01", "C4", "C5"]:
         ks = a.k or (list(wl.C4_K_VALUES) if config == "C4" else [None])

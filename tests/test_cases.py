@@ -24,7 +24,7 @@ def test_cases_help():
 @pytest.mark.gpu
 @pytest.mark.parametrize("config,k,rows", [("C1", None, 4), ("C2", None, 8), ("C3", None, 16),
                                            ("N01", None, 8), ("C4", 256, 12), ("C5", None, 6)])
-@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "f32"])
 def test_cases_line_and_parity(orc, config, k, rows, dtype):
     from batch_topk_b200 import cases
 
@@ -33,6 +33,15 @@ def test_cases_line_and_parity(orc, config, k, rows, dtype):
     json.dumps(line)
     assert line["segments"] == rows and line["status"] == 0
     assert line["kernel_us"] > 0 and line["call_us"] >= line["kernel_us"] * 0.5
+    if dtype == "f32":
+        xh = x.cpu().numpy().view(np.uint32)
+        if off is None:
+            ev, ei = orc.topk_f32(xh, line["k"])
+        else:
+            ev, ei = orc.topk_csr_f32(xh.reshape(-1), off, line["k"])
+        assert np.array_equal(oi.cpu().numpy(), ei)
+        assert np.array_equal(ov.cpu().numpy().view(np.uint32), ev)
+        return
     xh = x.cpu().numpy().view(np.uint16)
     if off is None:
         ev, ei = orc.topk(xh, line["k"], bf16=bf16)
