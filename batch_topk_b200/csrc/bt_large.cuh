@@ -360,8 +360,18 @@ __device__ bool large_chunk(const TopkParams& p, const StageInfo& si, const uint
   SCount c;
   bool counted = false;
   if (ls.K != kNoThreshold && !ls.rising) {
-    const CCount cc = contig_count<true>(si, buf, sm, ls.K, par);
+    CCount cc = contig_count<true>(si, buf, sm, ls.K, par);
     if (cc.fail) return false;
+    if (cc.total > C - ls.nbuf && ls.nbuf > k) {
+      // The cache's own k-th key is usually far tighter than anything this chunk certifies
+      // alone (the k-th of every value seen so far): cut to it and count again.
+      const uint32_t K1 = ls.K;
+      cut_to_k(sm, ls, k);
+      if (ls.K != K1) {
+        cc = contig_count<true>(si, buf, sm, ls.K, par);
+        if (cc.fail) return false;
+      }
+    }
     if (cc.total <= C - ls.nbuf) {
       if (cc.maxcnt <= kClusterMax) {
         contig_append<true>(si, buf, cc, ls.K, sm, ls.nbuf);

@@ -8,8 +8,9 @@ fire-emblem/batch_topk test/test_batch_topk.cu:
   :602-617  the 64-value final-sort case (42, 42, +inf, +inf, 17, 17, NaN, -inf, then -i).
 
 The libstdc++ float path is: one 32-bit draw u, s = float(u) / 2^32 (clamped below 1),
-value = s * (b - a) + a, all in float.  ``tests/test_golden.py`` checks these bit for bit
-against the same generators compiled from C++ (oracle/_ref) when that build is present.
+value = s * (b - a) + a, all in float.
+``tests/test_oracle.py::test_generators_match_reference_code`` checks these bit for bit against
+the same generators compiled from C++ (oracle/_ref) when that build is present.
 """
 from __future__ import annotations
 
