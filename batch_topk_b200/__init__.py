@@ -137,6 +137,37 @@ def batch_topk_half_noalloc(d_input: int, seg_num: int, seg_len: int, k: int,
                                             d_output_indices, stream)
 
 
+LOGITS_MAX_K = 64
+
+
+def logits_f16(d_hidden: int, d_weight: int, M: int, V: int, D: int, d_logits: int,
+               stream: int = 0) -> int:
+    """bt_logits_f16 (no reference counterpart): logits[M, V] = hidden[M, D] . weight[V, D]^T in
+    fp16 (fp32 accumulation on the tensor cores), stored row-major."""
+    return _lib.load().bt_logits_f16(d_hidden, d_weight, M, V, D, d_logits, stream)
+
+
+def logits_topk_f16_workspace_size(M: int, V: int, D: int, k: int) -> int:
+    return int(_lib.load().bt_logits_topk_f16_workspace_size(M, V, D, k))
+
+
+def logits_topk_f16(d_hidden: int, d_weight: int, M: int, V: int, D: int, k: int,
+                    d_output_values: int, d_output_indices: int, d_workspace: int,
+                    workspace_bytes: int, stream: int = 0) -> int:
+    """bt_logits_topk_f16 (no reference counterpart): the top k of each row of the logits that
+    logits_f16 would store, with batch_topk_half's order and layout, without storing them."""
+    return _lib.load().bt_logits_topk_f16(d_hidden, d_weight, M, V, D, k, d_output_values,
+                                          d_output_indices, d_workspace, workspace_bytes, stream)
+
+
+def logits_topk_status(d_workspace: int, M: int, V: int, D: int, k: int, stream: int = 0) -> int:
+    """Status flags of the last logits_topk_f16 call on this workspace (synchronous)."""
+    rc = int(_lib.load().bt_logits_topk_status(d_workspace, M, V, D, k, stream))
+    if rc < 0:
+        raise BatchTopkError(-rc, "bt_logits_topk_status")
+    return rc
+
+
 def workspace_status(d_workspace: int, seg_num: int = 0, stream: int = 0):
     """Synchronously reads the device status of the last call on this workspace.
 

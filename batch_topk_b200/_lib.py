@@ -27,6 +27,10 @@ EXPORTED = (
     "bt_topk_f32_segmented_workspace_size",
     "bt_workspace_status",
     "bt_noalloc_status",
+    "bt_logits_f16",
+    "bt_logits_topk_f16_workspace_size",
+    "bt_logits_topk_f16",
+    "bt_logits_topk_status",
     "bt_set_handoff_wait_tries",
     "bt_set_profile_events",
     "bt_device_info",
@@ -83,6 +87,14 @@ def load() -> C.CDLL:
         lib.bt_workspace_status.restype = i32
         lib.bt_noalloc_status.argtypes = [vp, C.POINTER(C.c_uint * 6)]
         lib.bt_noalloc_status.restype = i32
+        lib.bt_logits_f16.argtypes = [vp, vp, i32, i32, i32, vp, vp]
+        lib.bt_logits_f16.restype = i32
+        lib.bt_logits_topk_f16_workspace_size.argtypes = [i32, i32, i32, i32]
+        lib.bt_logits_topk_f16_workspace_size.restype = sz
+        lib.bt_logits_topk_f16.argtypes = [vp, vp, i32, i32, i32, i32, vp, vp, vp, sz, vp]
+        lib.bt_logits_topk_f16.restype = i32
+        lib.bt_logits_topk_status.argtypes = [vp, i32, i32, i32, i32, vp]
+        lib.bt_logits_topk_status.restype = i32
         lib.bt_set_handoff_wait_tries.argtypes = [i32]
         lib.bt_set_handoff_wait_tries.restype = None
         lib.bt_set_profile_events.argtypes = [vp, vp]

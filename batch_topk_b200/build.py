@@ -14,6 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 SRC = os.path.join(HERE, "csrc", "batch_topk.cu")
 GEN_SRC = os.path.join(HERE, "csrc", "gen.cu")  # device-side input generation
+LOGITS_SRC = os.path.join(HERE, "csrc", "bt_logits.cu")  # logits producer, fused top-k epilogue
 HEADERS = [os.path.join(HERE, "csrc", f) for f in ("bt_device.cuh", "bt_kernels.cuh", "bt_body.cuh",
                                                    "bt_elem.cuh", "bt_small.cuh",
                                                    "bt_large.cuh", "bt_common.cuh", "bt_f32.cuh")] + [
@@ -41,7 +42,7 @@ def up_to_date() -> bool:
     if not os.path.exists(LIB):
         return False
     t = os.path.getmtime(LIB)
-    return all(os.path.getmtime(p) <= t for p in [SRC, GEN_SRC, *HEADERS])
+    return all(os.path.getmtime(p) <= t for p in [SRC, GEN_SRC, LOGITS_SRC, *HEADERS])
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
@@ -49,7 +50,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return LIB
     os.makedirs(LIB_DIR, exist_ok=True)
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-o", tmp, SRC, GEN_SRC]
+    cmd = [nvcc(), *NVCC_FLAGS, "-o", tmp, SRC, GEN_SRC, LOGITS_SRC]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -143,6 +143,37 @@ int bt_workspace_status(const void* d_workspace, int seg_num, void* stream, unsi
  * Allocates nothing.  Returns the BT_STATUS_* flags, or a negated cudaError_t code. */
 int bt_noalloc_status(void* stream, unsigned* stats);
 
+/* Logits producer with the top-k fused into its epilogue; no reference counterpart (the
+ * reference selects from logits already in memory, include/batch_topk.cuh:10-19).
+ *
+ * logits[M, V] = hidden[M, D] . weight[V, D]^T: fp16 inputs (row-major, 16-byte aligned),
+ * fp32 accumulation on the tensor cores, rounded to fp16 (round to nearest even) -- the values
+ * a GEMM that stores fp16 logits produces.  1 <= M <= 128, V >= 1, D >= 8 with D % 8 == 0.
+ *
+ * bt_logits_f16 stores the logits, row-major [M, V] (2-byte aligned).
+ *
+ * bt_logits_topk_f16 returns, per row, the top k of those logits with the order and output
+ * layout of bt_topk_half (values descending, equal values by lower vocabulary index, NaN last;
+ * values are the fp16 logits' bit patterns, indices are vocabulary rows), without writing the
+ * logits to memory.  1 <= k <= min(BT_LOGITS_MAX_K, V).  The workspace (256-byte aligned) holds
+ * each CTA's per-row candidate lists and the second stage's scratch; its size comes from
+ * bt_logits_topk_f16_workspace_size (0: unsupported shape).  The results equal bt_topk_half
+ * applied to bt_logits_f16's output, bit for bit.
+ *
+ * bt_logits_topk_status reads back (synchronously) the status of the last call on a workspace:
+ * BT_STATUS_* flags, or a negated cudaError_t code. */
+#define BT_LOGITS_MAX_K 64
+int bt_logits_f16(const void* d_hidden, const void* d_weight, int M, int V, int D,
+                  void* d_logits, void* stream);
+
+size_t bt_logits_topk_f16_workspace_size(int M, int V, int D, int k);
+
+int bt_logits_topk_f16(const void* d_hidden, const void* d_weight, int M, int V, int D, int k,
+                       void* d_out_values, int* d_out_indices, void* d_workspace,
+                       size_t workspace_bytes, void* stream);
+
+int bt_logits_topk_status(const void* d_workspace, int M, int V, int D, int k, void* stream);
+
 /* Failure-path test hook (no reference counterpart): the number of tries each consumer <->
  * merger hand-off wait of the k <= 128 kernel makes before it gives up, for calls launched
  * after this one, process-wide.  0 makes those waits fail at once, so a call ends early with
