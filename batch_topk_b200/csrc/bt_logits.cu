@@ -164,7 +164,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 // most `target`: those are kept (at least k of them, so U is certified) and U << 16 is
 // returned -- unless ties at the k-th key leave more, when the exact cut is made.
 template <bool EXACT>
-__device__ __noinline__ uint32_t warp_cut_row(uint32_t* ent, uint16_t* vb, int n, int k,
+__device__ __forceinline__ uint32_t warp_cut_row(uint32_t* ent, uint16_t* vb, int n, int k,
                                                  int target, int* kept) {
   constexpr int NJ = kMaxCap / 32;
   const int lane = threadIdx.x & 31;
@@ -411,17 +411,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Each thread filters its own row's 32 values against the row's threshold (one
           // compare a value; appends are rare once the row has a threshold) ...
           if (r < p.M) {
-            uint32_t* re = ent + r * p.cap;
-            uint16_t* rb = vbits + r * p.cap;
+            // entries of all 32 values first (independent of one another), then the appends
             const uint32_t ob = static_cast<uint32_t>(col0 - colbase);
+            uint32_t e[32], hw2[16];
+            uint32_t pm = 0;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const uint32_t h = __half_as_ushort(__float2half_rn(__uint_as_float(v[j])));
-              const uint32_t e = (f16::desc_key(h) << 16) | (ob + static_cast<uint32_t>(j));
-              if (col0 + j < p.V && e < T) {
-                re[cnt] = e;
-                rb[cnt] = static_cast<uint16_t>(h);
-                ++cnt;
+            for (int j = 0; j < 32; j += 2) {
+              const __half2 h2 = __floats2half2_rn(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+              const uint32_t hw = *reinterpret_cast<const uint32_t*>(&h2);
+              hw2[j >> 1] = hw;
+              e[j] = (f16::desc_key(hw & 0xFFFFu) << 16) | (ob + static_cast<uint32_t>(j));
+              e[j + 1] = (f16::desc_key(hw >> 16) << 16) | (ob + static_cast<uint32_t>(j + 1));
+              pm |= (e[j] < T ? 1u : 0u) << j;
+              pm |= (e[j + 1] < T ? 1u : 0u) << (j + 1);
+            }
+            if (col0 + 32 > p.V) pm &= p.V > col0 ? (1u << (p.V - col0)) - 1u : 0u;
+            if (pm) {
+              uint32_t* re = ent + r * p.cap;
+              uint16_t* rb = vbits + r * p.cap;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if ((pm >> j) & 1u) {
+                  re[cnt] = e[j];
+                  rb[cnt] = static_cast<uint16_t>(hw2[j >> 1] >> (16 * (j & 1)));
+                  ++cnt;
+                }
               }
             }
           }
@@ -702,6 +716,7 @@ int bt_logits_topk_f16(const void* d_hidden, const void* d_weight, int M, int V,
   const int mpad = (M + 31) & ~31;
   p.cap = static_cast<int>(kBufBytes / (static_cast<size_t>(mpad) * 6));
   if (p.cap > kMaxCap) p.cap = kMaxCap;
+  p.cap = (p.cap - 1) | 1;  // odd: the rows' appends at equal counts fall in distinct banks
   if (p.cap < k + 32) return cudaErrorInvalidValue;  // cannot happen for M <= 128, k <= 64
   p.cand_vals = reinterpret_cast<uint16_t*>(ws + f.vals);
   p.cand_idx = reinterpret_cast<int*>(ws + f.idx);
