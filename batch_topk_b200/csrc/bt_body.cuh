@@ -463,6 +463,7 @@ topk_kernel(TopkParams p) {
     }
     fence_mbar_init();
     sm.fail = 0u;
+    if constexpr (BIG) sm.probe_req = 0u;
   }
   if (tid < 256) {
     sm.hist1[tid] = 0;
@@ -475,7 +476,11 @@ topk_kernel(TopkParams p) {
   grid_dep_launch();
   if (tid >= kThreads) {
     if (tid == kThreads) {
-      producer_loop<BIG>(p, stages, full, empty, info, &sm.fail);
+      if constexpr (BIG) {
+        producer_loop<BIG>(p, stages, full, empty, info, &sm.fail, &sm.probe_req);
+      } else {
+        producer_loop<BIG>(p, stages, full, empty, info, &sm.fail);
+      }
     } else if (!BIG && tid >= kThreads + 32) {
       if constexpr (!BIG) merger_loop(p, sm);
     }

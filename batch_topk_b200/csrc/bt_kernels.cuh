@@ -133,6 +133,7 @@ struct StageInfo {
   int vlo, vhi;    // chunk-relative vectors that straddle the segment ends (-1: none)
   int last;        // last chunk of this work part
   int part;        // work part id (kStopPart: no more work)
+  int probe;       // k > 128: a look at the segment's last chunk ahead of order (not its turn)
 };
 constexpr int kStopPart = -1;
 constexpr uint32_t kWorkCounter = 8;  // status[8]: next work part to claim (reset per call)
@@ -152,6 +153,7 @@ struct alignas(16) Scratch {
   uint32_t before1, before2;
   uint32_t bcast[4];
   uint32_t fail;
+  uint32_t probe_req;  // k > 128: part id + 1 whose segment's last chunk should be probed next
 };
 
 // k <= 128: per-segment state lives with the merger warp (bt_small.cuh).
@@ -258,7 +260,8 @@ __device__ __forceinline__ void decode_part(const TopkParams& p, long long part,
 // stages, a wait for a free stage gives up at once instead of running out its tries.
 template <bool BIG>
 __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* full,
-                              uint64_t* empty, StageInfo* info, const uint32_t* abort) {
+                              uint64_t* empty, StageInfo* info, const uint32_t* abort,
+                              const volatile uint32_t* probe_req = nullptr) {
   constexpr int S = Cfg<BIG>::kStagesN;
   const uint64_t policy = policy_evict_first();
   const long long nparts = total_parts(p);
@@ -302,6 +305,7 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
     si.nchunks = g.nchunks;
     si.chunk_vecs = g.chunk_vecs;
     si.last = last_c ? 1 : 0;
+    si.probe = 0;
     si.cv0 = g.v0 + static_cast<long long>(c) * g.chunk_vecs;
     const long long rem = g.v0 + g.nv - si.cv0;
     si.nvc = static_cast<int>(rem < g.chunk_vecs ? rem : g.chunk_vecs);
@@ -351,7 +355,19 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
       SegGeom g;
       long long slot0;
       decode_part(p, part, &s, &c0, &c1, &g, &slot0);
+      bool probed = false;
       for (int c = c0; c < c1 && ok; ++c) {
+        // k > 128: the consumers found this part's values rising chunk after chunk; the
+        // segment's last chunk goes in next, out of turn, so its certified threshold can stop
+        // the climb (it is read again in its own turn)
+        if (probe_req != nullptr && !probed && c + 2 < c1 &&
+            *probe_req == static_cast<uint32_t>(part) + 1u) {
+          StageInfo pi = chunk_info(s, g, slot0, g.nchunks - 1, static_cast<int>(part), false);
+          pi.probe = 1;
+          probed = true;
+          ok = put(pi);
+          if (!ok) break;
+        }
         ok = put(chunk_info(s, g, slot0, c, static_cast<int>(part), c == c1 - 1));
       }
       part = next;

@@ -349,8 +349,9 @@ __device__ bool large_chunk(const TopkParams& p, const StageInfo& si, const uint
                             LargeScratch& sm, LargeState& ls, int& par) {
   constexpr uint32_t C = Cfg<true>::kCacheCap;
   const uint32_t k = static_cast<uint32_t>(p.k);
+  const bool probe = si.probe != 0;
   // A chunk after a quiet one under a strict threshold: the maximum test and one OR-barrier.
-  if (ls.quiet && ls.K < kNoThreshold) {
+  if (!probe && ls.quiet && ls.K < kNoThreshold) {
     const uint32_t vb = key_to_bits(ls.K);
     uint32_t cnt;
     const uint32_t f = thread_flags<true>(si, buf, u32_as_h2(vb | (vb << 16)), false, &cnt);
@@ -359,7 +360,7 @@ __device__ bool large_chunk(const TopkParams& p, const StageInfo& si, const uint
   // Steady state: survivors under the segment's strict threshold, if the cache has room.
   SCount c;
   bool counted = false;
-  if (ls.K != kNoThreshold && !ls.rising) {
+  if (!probe && ls.K != kNoThreshold && !ls.rising) {
     CCount cc = contig_count<true>(si, buf, sm, ls.K, par);
     if (cc.fail) return false;
     if (cc.total > C - ls.nbuf && ls.nbuf > k) {
@@ -396,8 +397,28 @@ __device__ bool large_chunk(const TopkParams& p, const StageInfo& si, const uint
   // of its values have key <= kc).
   const uint32_t kc = chunk_select<true>(p, si, buf, sm);
   if (sm.fail) return false;
+  if (probe) {
+    // The segment's last chunk, out of turn: at least k of its values have key <= kc, and
+    // every value of this part precedes them, so this part's values with key <= kc (ties
+    // included) must stay candidates: the strict threshold kc + 1 (keys are integers).  The
+    // chunk is counted again in its own turn.
+    if (kc + 1u < kNoThreshold && kc + 1u < ls.K) {
+      ls.K = kc + 1u;
+      ls.strict = true;
+      ls.rising = false;
+      ls.quiet = false;
+      ls.added = 0;
+    }
+    return true;
+  }
   const bool own = kc != kNoThreshold && (ls.K == kNoThreshold || kc < ls.K);
+  const bool was_rising = ls.rising;
   ls.rising = (counted || ls.rising) && own;  // values ramp up: skip the stale count next time
+  if (ls.rising && !was_rising && threadIdx.x == 0 && ls.part_slot == ls.seg_slot) {
+    // ask the producer for a look at the segment's last chunk: on rising rows its certified
+    // threshold makes the chunks in between quiet
+    *reinterpret_cast<volatile uint32_t*>(&sm.probe_req) = static_cast<uint32_t>(ls.part) + 1u;
+  }
   // Every value with key <= kc, when the cache has room for them (the usual first chunk).
   // With less room than about k (rising rows after their first chunk) that seldom fits, and
   // the exact top k below is taken directly.
@@ -624,7 +645,7 @@ __device__ void consumer_loop_large(const TopkParams& p, uint8_t* stages, uint64
         failed = true;
         break;
       }
-      ++ls.mycnt;
+      if (!si.probe) ++ls.mycnt;
     }
     release_stage(&empty[st]);
     if (++st == S) {

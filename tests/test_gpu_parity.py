@@ -265,3 +265,42 @@ def test_back_to_back_calls_without_sync(orc):
             exp_v, exp_i = orc.topk_csr(bits.reshape(-1), off, k)
         assert_exact(ov.cpu().numpy().view(np.uint16), oi.cpu().numpy(), exp_v, exp_i,
                      f"call {n} ({op}, k={k})")
+
+
+def _rising_rows(seg_num, seg_len, seed):
+    """Rows whose values climb chunk after chunk (the k > 128 path probes such a segment's last
+    chunk out of turn), cycling over several kinds, one seed per row."""
+    rows = np.empty((seg_num, seg_len), np.uint16)
+    for i in range(seg_num):
+        rng = np.random.default_rng(seed + i)
+        kind = i % 6
+        if kind == 0:  # ascending N(0,1): fp16 ties near zero
+            r = np.sort(rng.standard_normal(seg_len)).astype(np.float16)
+        elif kind == 1:  # ascending plateaus: 64 levels
+            r = np.sort(rng.integers(0, 64, seg_len)).astype(np.float16)
+        elif kind == 2:  # ascending, then the last stretch falls: the probe's threshold is loose
+            r = np.sort(rng.standard_normal(seg_len)).astype(np.float16)
+            r[-(seg_len // 5):] = -r[-(seg_len // 5):]
+        elif kind == 3:  # rising sawtooth: each 16384-value stretch ascends, every stretch higher
+            t = (np.arange(seg_len) % 16384) / 16384.0 + np.arange(seg_len) // 16384
+            r = t.astype(np.float16)
+        elif kind == 4:  # ascending, the tail one repeated value (ties with the probe's certificate)
+            r = np.sort(rng.standard_normal(seg_len)).astype(np.float16)
+            r[-3000:] = r[-3000]
+        else:  # ascending with NaNs and -inf sprinkled in
+            r = np.sort(rng.standard_normal(seg_len)).astype(np.float16)
+            r[rng.random(seg_len) < 0.01] = np.float16(np.nan)
+            r[rng.random(seg_len) < 0.01] = np.float16(-np.inf)
+        rows[i] = r.view(np.uint16)
+    return rows
+
+
+@pytest.mark.parametrize("seg_len,k", [(70001, 129), (70001, 300), (131072, 513), (262144, 1024)])
+@pytest.mark.parametrize("misalign", [0, 3])
+def test_rising_rows_large_k(orc, seg_len, k, misalign):
+    # at least as many rows as resident blocks, so each block takes whole segments (the
+    # out-of-turn probe of a rising segment's last chunk happens on whole segments only)
+    x = _rising_rows(300, seg_len, 7 * seg_len + k)
+    exp_v, exp_i = orc.topk(x, k)
+    got_v, got_i = gpu_topk(x, k, misalign=misalign)
+    assert_exact(got_v, got_i, exp_v, exp_i, f"rising 300x{seg_len} k={k} +{misalign}")
