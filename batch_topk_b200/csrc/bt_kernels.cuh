@@ -355,20 +355,21 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
       SegGeom g;
       long long slot0;
       decode_part(p, part, &s, &c0, &c1, &g, &slot0);
+      // k > 128: when the consumers find this part's values rising chunk after chunk, the
+      // segment's last chunk goes in next, out of turn (once), so its certified threshold can
+      // stop the climb; it is read again in its own turn.  One copy of the stage fill serves
+      // both, which keeps this loop as short as without the probe.
       bool probed = false;
-      for (int c = c0; c < c1 && ok; ++c) {
-        // k > 128: the consumers found this part's values rising chunk after chunk; the
-        // segment's last chunk goes in next, out of turn, so its certified threshold can stop
-        // the climb (it is read again in its own turn)
-        if (probe_req != nullptr && !probed && c + 2 < c1 &&
-            *probe_req == static_cast<uint32_t>(part) + 1u) {
-          StageInfo pi = chunk_info(s, g, slot0, g.nchunks - 1, static_cast<int>(part), false);
-          pi.probe = 1;
-          probed = true;
-          ok = put(pi);
-          if (!ok) break;
-        }
-        ok = put(chunk_info(s, g, slot0, c, static_cast<int>(part), c == c1 - 1));
+      int c = c0;
+      while (ok && c < c1) {
+        const bool probe_now = probe_req != nullptr && !probed && c + 2 < c1 &&
+                               *probe_req == static_cast<uint32_t>(part) + 1u;
+        StageInfo si = chunk_info(s, g, slot0, probe_now ? g.nchunks - 1 : c,
+                                  static_cast<int>(part), !probe_now && c == c1 - 1);
+        si.probe = probe_now ? 1 : 0;
+        ok = put(si);
+        probed = probed || probe_now;
+        if (!probe_now) ++c;
       }
       part = next;
     }

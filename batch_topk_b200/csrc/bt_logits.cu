@@ -319,6 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_h = policy_evict_last();       // H is re-read for every tile
       int s = 0;
       uint32_t ph = 0;
+      long long issued = 0;
       for (int t = t0; t < t1 && !*fail; ++t) {
         for (int kt = 0; kt < p.ktiles; ++kt) {
           if (!bt::mbar_wait_abort(&empty[s], ph ^ 1u, fail)) {
@@ -329,11 +330,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           bt::mbar_arrive_expect_tx(&full[s], kStageBytes);
           tma_load_2d(st, &tmA, kt * kBK, 0, &full[s], pol_h);
           tma_load_2d(st + kTileABytes, &tmB, kt * kBK, t * kBN, &full[s], pol_w);
+          ++issued;
           if (++s == kStages) {
             s = 0;
             ph ^= 1u;
           }
         }
+      }
+      // Do not retire while a tensor copy may still land in shared memory (after a failure the
+      // consumer may not have waited for the last stages); a copy always completes.
+      for (long long r = issued - kStages; r < issued; ++r) {
+        if (r >= 0) bt::mbar_wait(&full[r % kStages], static_cast<uint32_t>((r / kStages) & 1));
       }
     }
   } else if (warp == 1) {

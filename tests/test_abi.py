@@ -115,3 +115,15 @@ def test_error_strings_and_version():
 def test_workspace_status_rejects_null():
     stats = (C.c_uint * 6)()
     assert _lib.load().bt_workspace_status(None, 0, None, C.byref(stats)) == INVALID
+
+
+def test_logits_argument_errors():
+    """The logits producer rejects null or misaligned pointers before any CUDA work."""
+    assert bt.logits_f16(0, FAKE, 4, 100, 64, FAKE, 0) == INVALID
+    assert bt.logits_f16(FAKE, 0, 4, 100, 64, FAKE, 0) == INVALID
+    assert bt.logits_f16(FAKE, FAKE, 4, 100, 64, 0, 0) == INVALID
+    assert bt.logits_f16(FAKE + 2, FAKE, 4, 100, 64, FAKE, 0) == INVALID  # not 16-byte aligned
+    assert bt.logits_f16(FAKE, FAKE, 4, 100, 64, FAKE + 1, 0) == INVALID  # not 2-byte aligned
+    assert bt.logits_topk_f16(0, FAKE, 4, 100, 64, 8, FAKE, FAKE, FAKE, 1 << 20, 0) == INVALID
+    assert bt.logits_topk_f16(FAKE, FAKE, 4, 100, 64, 8, FAKE, FAKE + 2, FAKE, 1 << 20, 0) == INVALID
+    assert bt.logits_topk_f16(FAKE, FAKE, 4, 100, 64, 8, FAKE, FAKE, FAKE + 16, 1 << 20, 0) == INVALID
