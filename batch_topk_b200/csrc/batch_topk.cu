@@ -217,9 +217,10 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, Elem e
     p.parts_total = static_cast<long long>(p.seg_num) * per;
     parts = p.parts_total;
     // Whole segments: claim chunk by chunk and let blocks that run dry help (BT_STEAL=0: off).
-    // Only for k <= 128, whose first chunk of a visit is cheap; for larger k a helper's first
-    // chunk (select plus exact select) costs more than the chunks it takes over.
-    p.steal = (!big && per == 1 && g_steal_env != 0) ? 1 : 0;
+    // 16-bit inputs: for k > 128 a helper's first chunk (a select, often an exact select)
+    // costs more, so it joins only segments with more chunks left.
+    p.steal = (!f32 && per == 1 && g_steal_env != 0) ? 1 : 0;
+    p.help_min = big ? kHelpMinChunksBig : kHelpMinChunks;
   }
   if (csr) {
     e = launch_setup(csr_prep_kernel, p, 1, 1024, stream);

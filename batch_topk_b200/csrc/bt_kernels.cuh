@@ -61,12 +61,15 @@ struct TopkParams {
   int part_chunks;               // at most this many chunks per work part
   int steal;                     // whole segments, chunks claimed one by one, idle blocks help
   int help_window;               // how many of the last-claimed segments idle blocks may help
+  int help_min;                  // a helper joins a segment with at least this many chunks left
   uint32_t* chunk_next;          // [seg_num] next unclaimed chunk of each segment (steal)
   int k;
   int groups;                    // group maxima per thread in the threshold select
   int cap;                       // candidate capacity per chunk slot
   int stats;                     // count events into status[1..4]
-  uint32_t* seg_thresh;          // [seg_num] thresholds shared by CTAs splitting a segment
+  uint32_t* seg_thresh;          // [seg_num] the running strict threshold of the segment's
+                                 // first part and the last chunk it covers, (key << 16) | chunk
+                                 // (kNoOwnerKey: none yet), for the segment's other parts
   uint32_t* seg_done;            // [seg_num] chunks finished (arrival counter)
   uint32_t* chunk_count;         // [slot_capacity]
   uint32_t* chunk_off;           // [slot_capacity] merge scratch for very long segments
@@ -134,11 +137,23 @@ struct StageInfo {
   int last;        // last chunk of this work part
   int part;        // work part id (kStopPart: no more work)
   int probe;       // k > 128: a look at the segment's last chunk ahead of order (not its turn)
+  uint32_t ext_k;  // a strict threshold for this chunk certified by the segment's first part
+                   // (k values with key <= it at lower indices), or kNoThreshold
 };
 constexpr int kStopPart = -1;
+constexpr uint32_t kNoOwnerKey = 0xFFFFFFFFu;  // seg_thresh: the first part has no k-th key yet
+
+// The strict threshold a chunk c of another part may take from the first part's published
+// (key << 16) | last_chunk word: the k values behind the key lie in chunks <= last_chunk, so
+// they precede every value of chunk c when last_chunk < c (ties at the key lose by index).
+__device__ __forceinline__ uint32_t owner_threshold(uint32_t word, int c) {
+  const uint32_t key = word >> 16;
+  return (key < kNoThreshold && (word & 0xFFFFu) < static_cast<uint32_t>(c)) ? key : kNoThreshold;
+}
 constexpr uint32_t kWorkCounter = 8;  // status[8]: next work part to claim (reset per call)
 constexpr uint32_t kHelpCounter = 9;  // status[9]: next segment an idle block helps
-constexpr int kHelpMinChunks = 3;     // a helper joins a segment with at least this many left
+constexpr int kHelpMinChunks = 3;     // k <= 128: a helper joins a segment with >= 3 chunks left
+constexpr int kHelpMinChunksBig = 8;  // k > 128 (a costlier first chunk of a visit)
 
 template <bool BIG>
 struct alignas(16) Scratch {
@@ -168,6 +183,7 @@ struct BatchMeta {
   int flags;            // kBatchEnd | kBatchStop
   int mycnt;            // chunks of the segment in this block's part, up to this batch
   int nchunks;
+  int c;                // the chunk this batch comes from
   uint32_t K;           // consumers' threshold for the segment
 };
 constexpr int kBatchEnd = 1;
@@ -269,13 +285,16 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
   int st = 0;     // stage of the next load
   int round = 0;  // how many times every stage has been filled
   bool ok = true;
-  // one stage: wait for it to be free, fill its info, start the copy (or just signal)
-  auto put = [&](const StageInfo& si) -> bool {
+  // one stage: wait for it to be free, fill its info, start the copy (or just signal).  `ow`
+  // is the segment's published first-part word for another part's chunk (kNoOwnerKey: none);
+  // its load was issued before the call, so the round trip overlaps the wait for the stage.
+  auto put = [&](StageInfo si, uint32_t ow) -> bool {
     if (round > 0 && !mbar_wait_abort(&empty[st], static_cast<uint32_t>((round - 1) & 1),
                                       abort)) {
       atomicOr(&p.status[0], kStatusWaitTimeout);
       return false;
     }
+    si.ext_k = owner_threshold(ow, si.c);
     info[st] = si;
     if (si.nvc > 0) {
       fence_proxy_async_smem();
@@ -306,6 +325,7 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
     si.chunk_vecs = g.chunk_vecs;
     si.last = last_c ? 1 : 0;
     si.probe = 0;
+    si.ext_k = kNoThreshold;
     si.cv0 = g.v0 + static_cast<long long>(c) * g.chunk_vecs;
     const long long rem = g.v0 + g.nv - si.cv0;
     si.nvc = static_cast<int>(rem < g.chunk_vecs ? rem : g.chunk_vecs);
@@ -320,28 +340,55 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
     // Whole segments, claimed in order.  A segment's chunks are claimed one at a time (one
     // ahead, so the claim's latency hides behind the stage wait).  Once every segment is
     // claimed, a block that has run dry helps one of the segments claimed last: it takes
-    // the chunks the owner has not claimed yet, and the split-segment merge joins the two
-    // lists.  Each visit of a block to a segment is one work part (numbered per block).
+    // the chunks the owner has not claimed yet, one at a time as well, so the two share out
+    // what is left at the pace each works at, and the split-segment merge joins the two
+    // lists (their chunks interleave).  Each visit of a block to a segment is one work part
+    // (numbered per block).
     int visit = 0;
     long long s = atomicAdd(&p.status[kWorkCounter], 1u);
     bool own = true;
     while (ok) {
       if (s >= p.seg_num) {
         own = false;
+        // k > 128: help only once this block's consumers are through every stage filled so
+        // far (a part's close there takes long): a chunk claimed earlier would wait in a stage
+        // while the owner could have taken it.
+        if (BIG && issued > 0) {
+          const int last = st == 0 ? S - 1 : st - 1;
+          const int rl = st == 0 ? round - 1 : round;  // the round that filled it
+          if (!mbar_wait_abort(&empty[last], static_cast<uint32_t>(rl & 1), abort)) {
+            atomicOr(&p.status[0], kStatusWaitTimeout);
+            ok = false;
+            break;
+          }
+        }
         const long long h = atomicAdd(&p.status[kHelpCounter], 1u);
         if (h >= p.help_window) break;
         s = p.seg_num - 1 - h;
       }
       const SegGeom g = seg_geom(p, static_cast<int>(s));
       const long long slot0 = s * p.p_max;
-      if (!own && static_cast<int>(__ldcg(&p.chunk_next[s])) + kHelpMinChunks > g.nchunks) {
+      if (!own && static_cast<int>(__ldcg(&p.chunk_next[s])) + p.help_min > g.nchunks) {
         s = p.seg_num;  // too little left to repay a helper's first chunk: try the next one
         continue;
       }
       int c = static_cast<int>(atomicAdd(&p.chunk_next[s], 1u));
+      bool probed = false;
       while (ok && c < g.nchunks) {
+        // k > 128: the owner's consumers found the values rising; the segment's last chunk
+        // goes in next, out of turn (once, unclaimed: it is read again in its turn)
+        if (probe_req != nullptr && !probed && c + 2 < g.nchunks &&
+            *probe_req == static_cast<uint32_t>(visit) + 1u) {
+          StageInfo si = chunk_info(static_cast<int>(s), g, slot0, g.nchunks - 1, visit, false);
+          si.probe = 1;
+          ok = put(si, kNoOwnerKey);
+          probed = true;
+          continue;
+        }
+        // a helper reads the owner's latest threshold with each claim (both round trips overlap)
+        const uint32_t ow = own ? kNoOwnerKey : ld_relaxed_gpu(&p.seg_thresh[s]);
         const int cn = static_cast<int>(atomicAdd(&p.chunk_next[s], 1u));
-        ok = put(chunk_info(static_cast<int>(s), g, slot0, c, visit, cn >= g.nchunks));
+        ok = put(chunk_info(static_cast<int>(s), g, slot0, c, visit, cn >= g.nchunks), ow);
         c = cn;
       }
       ++visit;
@@ -367,7 +414,9 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
         StageInfo si = chunk_info(s, g, slot0, probe_now ? g.nchunks - 1 : c,
                                   static_cast<int>(part), !probe_now && c == c1 - 1);
         si.probe = probe_now ? 1 : 0;
-        ok = put(si);
+        // a later part's chunks after its first may take the first part's threshold
+        const bool ext = c0 > 0 && c > c0;
+        ok = put(si, ext ? ld_relaxed_gpu(&p.seg_thresh[s]) : kNoOwnerKey);
         probed = probed || probe_now;
         if (!probe_now) ++c;
       }
@@ -379,7 +428,7 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
     z.s = -1;
     z.part = kStopPart;
     z.vlo = z.vhi = -1;
-    ok = put(z);
+    ok = put(z, kNoOwnerKey);
   }
   // Do not retire while a bulk copy may still land in this block's shared memory.
   for (long long r = issued - S; r < issued; ++r) {
@@ -537,7 +586,7 @@ __global__ void init_kernel(TopkParams p) {
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   if (i < 16) p.status[i] = 0;
   for (long long s = i; s < p.seg_num; s += stride) {
-    p.seg_thresh[s] = kNoThreshold;
+    p.seg_thresh[s] = kNoOwnerKey;
     p.seg_done[s] = 0;
     if (p.steal) p.chunk_next[s] = 0;
   }
@@ -560,7 +609,7 @@ __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
     const int s = base + tid;
     uint32_t nch = 0;
     if (s < p.seg_num) {
-      p.seg_thresh[s] = kNoThreshold;
+      p.seg_thresh[s] = kNoOwnerKey;
       p.seg_done[s] = 0;
       nch = static_cast<uint32_t>(seg_geom(p, s).nchunks);
       if (p.offsets[s] < 0 || p.offsets[s + 1] < p.offsets[s]) {

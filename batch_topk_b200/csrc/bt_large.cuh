@@ -29,6 +29,7 @@ struct LargeState {
   long long part_slot = 0;    // slot of the part's first chunk: its partial list lives there
   long long seg_slot = 0;     // slot of the segment's chunk 0
   long long a0 = 0, a1 = 0;   // aligned element coordinates of the segment
+  uint32_t pub = kNoThreshold;  // thread 0 of a first part: the threshold it last published
 };
 
 // ---- strided count and append --------------------------------------------------------
@@ -554,6 +555,41 @@ __device__ __forceinline__ void load_list(const unsigned long long* src, uint32_
   for (uint32_t i = threadIdx.x; i < n; i += kThreads) sm.cache[at + i] = __ldcg(src + i);
 }
 
+// Merges the adjacent runs sm.cache[0, n) and sm.cache[n, n + m), each in index order, into
+// one run in index order: each entry moves to its own position plus the number of entries of
+// the other run with a smaller index (a binary search; indices are distinct).  Each thread
+// holds its kCacheCap / kThreads entries in registers across the barrier, so the in-place
+// writes never overtake a read.
+__device__ void merge_index_runs(LargeScratch& sm, uint32_t n, uint32_t m) {
+  constexpr int kPer = Cfg<true>::kCacheCap / kThreads;
+  const uint32_t tot = n + m;
+  unsigned long long v[kPer];
+  uint32_t pos[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const uint32_t i = threadIdx.x * kPer + j;
+    v[j] = i < tot ? sm.cache[i] : 0ull;
+    pos[j] = i;
+    if (i < tot) {
+      const bool first = i < n;
+      const uint32_t base = first ? n : 0u;
+      const uint32_t idx = static_cast<uint32_t>(v[j] >> 16);
+      uint32_t lo = 0, hi = first ? m : n;  // entries of the other run with a smaller index
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (static_cast<uint32_t>(sm.cache[base + mid] >> 16) < idx) lo = mid + 1u; else hi = mid;
+      }
+      pos[j] = (first ? i : i - n) + lo;
+    }
+  }
+  csync();
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    if (threadIdx.x * kPer + j < tot) sm.cache[pos[j]] = v[j];
+  }
+  csync();
+}
+
 // End of this block's part of segment ls.s: write the row, or publish the part's top k and,
 // if this block finishes the segment, merge all parts in index order.
 __device__ void large_close(const TopkParams& p, LargeState& ls, LargeScratch& sm) {
@@ -583,7 +619,7 @@ __device__ void large_close(const TopkParams& p, LargeState& ls, LargeScratch& s
   csync();
   if (!sm.bcast[0]) return;
   __threadfence();
-  // last to arrive: every part's list, in slot (= index) order
+  // last to arrive: every part's list, joined in index order
   uint32_t n = 0;
   for (int c0 = 0; c0 < ls.nchunks; c0 += kThreads) {
     const int c = c0 + tid;
@@ -601,8 +637,11 @@ __device__ void large_close(const TopkParams& p, LargeState& ls, LargeScratch& s
       }
       load_list(reinterpret_cast<const unsigned long long*>(p.cand + (ls.seg_slot + c0 + j) * p.cap),
                 cj, sm, n);
-      n += cj;
       csync();
+      // parts that took turns at a segment's chunks (helping) hold interleaved index ranges:
+      // the lists meet by index, as the cuts and the tie rule need
+      if (p.steal && n > 0) merge_index_runs(sm, n, cj);
+      n += cj;
     }
     csync();  // tbase is rewritten by the next round
   }
@@ -641,11 +680,25 @@ __device__ void consumer_loop_large(const TopkParams& p, uint8_t* stages, uint64
     }
     if (si.nvc > 0) {
       const uint8_t* buf = stages + static_cast<size_t>(st) * kStageBytes;
+      // another part's chunk: the segment's first part may have certified a tighter strict
+      // threshold from chunks that all precede this one
+      if (si.ext_k < ls.K) {
+        ls.K = si.ext_k;
+        ls.strict = true;
+      }
       if (!large_chunk(p, si, buf, sm, ls, par)) {
         failed = true;
         break;
       }
       if (!si.probe) ++ls.mycnt;
+      // the segment's first part publishes its threshold for helpers, with the last chunk
+      // it covers (strict K: k values with key <= K lie in chunks <= si.c, or, from a probe
+      // of the last chunk, anywhere with key < K, which bounds every chunk)
+      if (threadIdx.x == 0 && !si.probe && ls.part_slot == ls.seg_slot &&
+          ls.mycnt < ls.nchunks && ls.K < kNoThreshold && ls.K != ls.pub) {
+        st_relaxed_gpu(&p.seg_thresh[ls.s], (ls.K << 16) | static_cast<uint32_t>(si.c));
+        ls.pub = ls.K;
+      }
     }
     release_stage(&empty[st]);
     if (++st == S) {

@@ -214,6 +214,7 @@ __device__ int small_chunk(const TopkParams& p, const StageInfo& si, const uint8
   meta.flags = si.last ? kBatchEnd : 0;
   meta.mycnt = ss.mycnt + 1;
   meta.nchunks = si.nchunks;
+  meta.c = si.c;
   meta.K = ss.K;
   send_batch(sm, b, meta);
   *nbp = nb + 1;
@@ -249,6 +250,14 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
         ss.slot0 = si.slot;  // first slot of this part
       }
       const uint8_t* buf = stages + static_cast<size_t>(st) * kStageBytes;
+      // The segment's first part certified a strict threshold for this chunk (another part):
+      // take it when it is at least as tight as this part's own.
+      bool adopted = false;
+      if (si.ext_k < ss.K || (si.ext_k == ss.K && !ss.strict && si.ext_k < kNoThreshold)) {
+        ss.K = si.ext_k;
+        ss.strict = true;
+        adopted = ss.mycnt == 0;
+      }
       // Fast path for a middle chunk after a quiet one under a strict threshold: the max test
       // and one OR-barrier; only when some value passes (or a wait failed) does the chunk go
       // through the full count/compaction below.
@@ -260,7 +269,7 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
       const bool second = ss.mycnt == 1 && !ss.quiet;
       bool try_second = second && second_hot;
       if (second && !second_hot) second_hot = true;  // skipped once: the next part tries again
-      if (ss.strict && ss.K < kNoThreshold && (ss.quiet || try_second)) {
+      if (ss.strict && ss.K < kNoThreshold && (ss.quiet || try_second || adopted)) {
         const bool last = si.last != 0;  // read before the barrier
         const uint32_t vb = key_to_bits(ss.K);
         uint32_t cnt;
@@ -282,6 +291,7 @@ __device__ void consumer_loop_small(const TopkParams& p, uint8_t* stages, uint64
           meta.flags = kBatchEnd;
           meta.mycnt = ss.mycnt + 1;
           meta.nchunks = si.nchunks;
+          meta.c = si.c;
           meta.K = ss.K;
           send_batch(sm, static_cast<int>(nb & 1), meta);
           ++nb;
@@ -440,8 +450,6 @@ __device__ void finalize_part(const TopkParams& p, const BatchMeta& m, unsigned 
   __syncwarp();
   int last = 0;
   if (lane == 0) {
-    if (m.K < kNoThreshold) atomicMin(&p.seg_thresh[m.s], m.K);
-    __threadfence();
     const uint32_t old = atomicAdd(&p.seg_done[m.s], static_cast<uint32_t>(m.mycnt));
     last = old + static_cast<uint32_t>(m.mycnt) == static_cast<uint32_t>(m.nchunks);
   }
@@ -506,6 +514,12 @@ __device__ void merger_loop_r(const TopkParams& p, SmallScratch& sm) {
         *reinterpret_cast<volatile unsigned long long*>(&sm.kpub) =
             (static_cast<unsigned long long>(static_cast<uint32_t>(m.s)) << 32) |
             static_cast<uint32_t>(kth >> 48);
+        // the segment's first part also publishes it for the other parts (helpers), with the
+        // last chunk it covers: their later chunks may take it as a strict threshold
+        if (m.part_slot == m.seg_slot && m.mycnt < m.nchunks) {
+          st_relaxed_gpu(&p.seg_thresh[m.s],
+                         (static_cast<uint32_t>(kth >> 48) << 16) | static_cast<uint32_t>(m.c));
+        }
       }
     }
     if (m.flags & kBatchEnd) {
