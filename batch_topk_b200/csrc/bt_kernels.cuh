@@ -153,7 +153,7 @@ __device__ __forceinline__ uint32_t owner_threshold(uint32_t word, int c) {
 constexpr uint32_t kWorkCounter = 8;  // status[8]: next work part to claim (reset per call)
 constexpr uint32_t kHelpCounter = 9;  // status[9]: next segment an idle block helps
 constexpr int kHelpMinChunks = 3;     // k <= 128: a helper joins a segment with >= 3 chunks left
-constexpr int kHelpMinChunksBig = 8;  // k > 128 (a costlier first chunk of a visit)
+constexpr int kHelpMinChunksBig = 12;  // k > 128 (a costlier first chunk of a visit)
 
 template <bool BIG>
 struct alignas(16) Scratch {

@@ -304,3 +304,37 @@ def test_rising_rows_large_k(orc, seg_len, k, misalign):
     exp_v, exp_i = orc.topk(x, k)
     got_v, got_i = gpu_topk(x, k, misalign=misalign)
     assert_exact(got_v, got_i, exp_v, exp_i, f"rising 300x{seg_len} k={k} +{misalign}")
+
+
+def _tail_rows(seg_num, seg_len, seed):
+    """More rows than resident blocks (so blocks take whole rows and, once every row is
+    claimed, idle blocks help the last ones), of uneven cost: heavy ties on a few levels (the
+    helper's and the owner's lists hold ties at the cutoff that only the index order ranks),
+    i.i.d. N(0,1), ascending rows, and constant rows."""
+    rows = np.empty((seg_num, seg_len), np.uint16)
+    for i in range(seg_num):
+        rng = np.random.default_rng(seed + i)
+        kind = i % 4
+        if kind == 0:
+            r = rng.integers(0, 16, seg_len).astype(np.float16)
+        elif kind == 1:
+            r = rng.standard_normal(seg_len).astype(np.float16)
+        elif kind == 2:
+            r = np.sort(rng.standard_normal(seg_len)).astype(np.float16)
+        else:
+            r = np.full(seg_len, 1.5, np.float16)
+        rows[i] = r.view(np.uint16)
+    return rows
+
+
+@pytest.mark.parametrize("k", [50, 256, 1024])
+@pytest.mark.parametrize("misalign", [0, 3])
+def test_tail_helpers(orc, k, misalign):
+    # 700 rows of 12 chunks: the last rows claimed are shared with blocks that ran dry, whose
+    # chunks interleave with the owner's; the split merge and the shared thresholds must give
+    # the single-block answer bit for bit
+    seg_len = 12 * 16384 - 5
+    x = _tail_rows(700, seg_len, 31 * k + misalign)
+    exp_v, exp_i = orc.topk(x, k)
+    got_v, got_i = gpu_topk(x, k, misalign=misalign)
+    assert_exact(got_v, got_i, exp_v, exp_i, f"tail 700x{seg_len} k={k} +{misalign}")
