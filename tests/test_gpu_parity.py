@@ -330,11 +330,11 @@ def _tail_rows(seg_num, seg_len, seed):
 @pytest.mark.parametrize("k", [50, 256, 1024])
 @pytest.mark.parametrize("misalign", [0, 3])
 def test_tail_helpers(orc, k, misalign):
-    # 700 rows of 12 chunks: the last rows claimed are shared with blocks that ran dry, whose
-    # chunks interleave with the owner's; the split merge and the shared thresholds must give
-    # the single-block answer bit for bit
-    seg_len = 12 * 16384 - 5
-    x = _tail_rows(700, seg_len, 31 * k + misalign)
+    # 600 rows of 20 chunks (k > 128 helpers need 12 unclaimed): the last rows claimed are
+    # shared with blocks that ran dry, whose chunks interleave with the owner's; the split merge
+    # and the shared thresholds must give the single-block answer bit for bit
+    seg_len = 20 * 16384 - 5
+    x = _tail_rows(600, seg_len, 31 * k + misalign)
     exp_v, exp_i = orc.topk(x, k)
     got_v, got_i = gpu_topk(x, k, misalign=misalign)
-    assert_exact(got_v, got_i, exp_v, exp_i, f"tail 700x{seg_len} k={k} +{misalign}")
+    assert_exact(got_v, got_i, exp_v, exp_i, f"tail 600x{seg_len} k={k} +{misalign}")
