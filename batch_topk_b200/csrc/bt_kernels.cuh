@@ -345,7 +345,10 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
     // lists (their chunks interleave).  Each visit of a block to a segment is one work part
     // (numbered per block).
     int visit = 0;
-    long long s = atomicAdd(&p.status[kWorkCounter], 1u);
+    // the first segment of block b is segment b (no claim round trip before the first load;
+    // the grid never exceeds the segments here); later ones come from the work counter
+    const long long b0 = static_cast<long long>(blockIdx.x);
+    long long s = b0 < p.seg_num ? b0 : static_cast<long long>(p.seg_num);
     bool own = true;
     while (ok) {
       if (s >= p.seg_num) {
@@ -362,9 +365,10 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
             break;
           }
         }
+        // k > 128 (rows of very uneven cost) walks the window twice: a second helper may join
         const long long h = atomicAdd(&p.status[kHelpCounter], 1u);
-        if (h >= p.help_window) break;
-        s = p.seg_num - 1 - h;
+        if (h >= (BIG ? 2 : 1) * static_cast<long long>(p.help_window)) break;
+        s = p.seg_num - 1 - h % p.help_window;
       }
       const SegGeom g = seg_geom(p, static_cast<int>(s));
       const long long slot0 = s * p.p_max;
@@ -372,7 +376,9 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
         s = p.seg_num;  // too little left to repay a helper's first chunk: try the next one
         continue;
       }
-      int c = static_cast<int>(atomicAdd(&p.chunk_next[s], 1u));
+      // the first claim takes two chunks: the first load waits for one round trip, not two
+      int c = static_cast<int>(atomicAdd(&p.chunk_next[s], 2u));
+      int pre = c + 1;  // claimed with c (past the end when c is the last chunk)
       bool probed = false;
       while (ok && c < g.nchunks) {
         // k > 128: the owner's consumers found the values rising; the segment's last chunk
@@ -387,12 +393,16 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
         }
         // a helper reads the owner's latest threshold with each claim (both round trips overlap)
         const uint32_t ow = own ? kNoOwnerKey : ld_relaxed_gpu(&p.seg_thresh[s]);
-        const int cn = static_cast<int>(atomicAdd(&p.chunk_next[s], 1u));
+        int cn = pre;
+        if (pre < 0) cn = static_cast<int>(atomicAdd(&p.chunk_next[s], 1u));
+        pre = -1;
         ok = put(chunk_info(static_cast<int>(s), g, slot0, c, visit, cn >= g.nchunks), ow);
         c = cn;
       }
       ++visit;
-      s = own ? static_cast<long long>(atomicAdd(&p.status[kWorkCounter], 1u)) : p.seg_num;
+      s = own ? static_cast<long long>(gridDim.x) +
+                    static_cast<long long>(atomicAdd(&p.status[kWorkCounter], 1u))
+              : p.seg_num;
     }
   } else {
     long long part = atomicAdd(&p.status[kWorkCounter], 1u);
