@@ -39,7 +39,7 @@ struct Layout {
   size_t status, thresh, done, next, chunk_start, part_start, counts, offs, cand, total;
 };
 
-// status | seg_thresh | seg_done | chunk_next (fixed-length) | chunk_start, part_start (CSR) |
+// status | seg_thresh | seg_done | chunk_next | chunk_start, part_start (CSR) |
 // chunk_count | chunk_off | candidates, each region 256-byte aligned.
 Layout make_layout(long long seg_num, long long slots, int cap, bool csr) {
   Layout L{};
@@ -52,7 +52,7 @@ Layout make_layout(long long seg_num, long long slots, int cap, bool csr) {
   L.status = take(16 * sizeof(uint32_t));
   L.thresh = take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
   L.done = take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
-  L.next = csr ? 0 : take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
+  L.next = take(static_cast<size_t>(seg_num) * sizeof(uint32_t));
   L.chunk_start = csr ? take(static_cast<size_t>(seg_num + 1) * sizeof(uint32_t)) : 0;
   L.part_start = csr ? take(static_cast<size_t>(seg_num + 1) * sizeof(uint32_t)) : 0;
   L.counts = take(static_cast<size_t>(slots) * sizeof(uint32_t));
@@ -212,16 +212,20 @@ cudaError_t launch_pipeline(TopkParams p, bool csr, long long work_items, Elem e
   const long long resident = static_cast<long long>(di.sms) * di.blocks_per_sm[kind];
   p.part_chunks = choose_part_chunks(work_items, p.seg_num, resident);
   long long parts = work_items;  // CSR: an upper bound (every part holds a chunk)
+  // CSR parts are whole segments when there are at least as many segments as resident blocks
+  bool whole = p.part_chunks == kMaxChunksPerSegment;
   if (!csr) {
     const long long per = (p.p_max + p.part_chunks - 1) / p.part_chunks;
     p.parts_total = static_cast<long long>(p.seg_num) * per;
     parts = p.parts_total;
-    // Whole segments: claim chunk by chunk and let blocks that run dry help (BT_STEAL=0: off).
-    // 16-bit inputs: for k > 128 a helper's first chunk (a select, often an exact select)
-    // costs more, so it joins only segments with more chunks left.
-    p.steal = (!f32 && per == 1 && g_steal_env != 0) ? 1 : 0;
-    p.help_min = big ? kHelpMinChunksBig : kHelpMinChunks;
+    whole = per == 1;
   }
+  // Whole segments: claim chunk by chunk and let blocks that run dry help (BT_STEAL=0: off).
+  // 16-bit inputs: for k > 128 a helper's first chunk (a select, often an exact select)
+  // costs more, so it joins only segments with more chunks left.  With whole segments the
+  // grid never exceeds the segments.
+  p.steal = (!f32 && whole && g_steal_env != 0) ? 1 : 0;
+  p.help_min = big ? kHelpMinChunksBig : kHelpMinChunks;
   if (csr) {
     e = launch_setup(csr_prep_kernel, p, 1, 1024, stream);
   } else {

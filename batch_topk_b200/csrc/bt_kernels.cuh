@@ -350,6 +350,9 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
     const long long b0 = static_cast<long long>(blockIdx.x);
     long long s = b0 < p.seg_num ? b0 : static_cast<long long>(p.seg_num);
     bool own = true;
+    // CSR: the set-up kernel clears the part count when the offsets are invalid (or every
+    // segment is empty): then no segment is touched
+    if (p.offsets && p.part_start[p.seg_num] == 0u) ok = false;
     while (ok) {
       if (s >= p.seg_num) {
         own = false;
@@ -371,7 +374,7 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
         s = p.seg_num - 1 - h % p.help_window;
       }
       const SegGeom g = seg_geom(p, static_cast<int>(s));
-      const long long slot0 = s * p.p_max;
+      const long long slot0 = p.offsets ? static_cast<long long>(p.chunk_start[s]) : s * p.p_max;
       if (!own && static_cast<int>(__ldcg(&p.chunk_next[s])) + p.help_min > g.nchunks) {
         s = p.seg_num;  // too little left to repay a helper's first chunk: try the next one
         continue;
@@ -621,6 +624,7 @@ __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
     if (s < p.seg_num) {
       p.seg_thresh[s] = kNoOwnerKey;
       p.seg_done[s] = 0;
+      if (p.steal) p.chunk_next[s] = 0;
       nch = static_cast<uint32_t>(seg_geom(p, s).nchunks);
       if (p.offsets[s] < 0 || p.offsets[s + 1] < p.offsets[s]) {
         atomicOr(&p.status[0], kStatusBadOffsets);
