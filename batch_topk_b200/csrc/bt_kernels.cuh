@@ -617,35 +617,51 @@ __global__ void __launch_bounds__(1024) csr_prep_kernel(TopkParams p) {
   if (tid < 16) p.status[tid] = 0;
   for (long long c = tid; c < p.slot_capacity; c += 1024) p.chunk_count[c] = 0;
   __syncthreads();
+  // Each thread takes kPrepPer consecutive segments a round (C4's 4096 segments: one round of
+  // two block scans, not four): the offsets' loads are in flight together.
+  constexpr int kPrepPer = 4;
   uint32_t carry = 0, pcarry = 0;
-  for (int base = 0; base < p.seg_num; base += 1024) {
-    const int s = base + tid;
-    uint32_t nch = 0;
-    if (s < p.seg_num) {
-      p.seg_thresh[s] = kNoOwnerKey;
-      p.seg_done[s] = 0;
-      if (p.steal) p.chunk_next[s] = 0;
-      nch = static_cast<uint32_t>(seg_geom(p, s).nchunks);
-      if (p.offsets[s] < 0 || p.offsets[s + 1] < p.offsets[s]) {
-        atomicOr(&p.status[0], kStatusBadOffsets);
-      }
-      if (nch == 0) {
-        for (int r = 0; r < p.k; ++r) {
-          const long long o = static_cast<long long>(s) * p.k + r;
-          if (p.out_values32) p.out_values32[o] = p.pad_bits;
-          else p.out_values[o] = static_cast<uint16_t>(p.pad_bits);
-          p.out_indices[o] = -1;
+  for (int base = 0; base < p.seg_num; base += 1024 * kPrepPer) {
+    uint32_t nch[kPrepPer];
+    uint32_t csum = 0, psum = 0;
+#pragma unroll
+    for (int r = 0; r < kPrepPer; ++r) {
+      const int s = base + tid * kPrepPer + r;
+      nch[r] = 0;
+      if (s < p.seg_num) {
+        p.seg_thresh[s] = kNoOwnerKey;
+        p.seg_done[s] = 0;
+        if (p.steal) p.chunk_next[s] = 0;
+        nch[r] = static_cast<uint32_t>(seg_geom(p, s).nchunks);
+        if (p.offsets[s] < 0 || p.offsets[s + 1] < p.offsets[s]) {
+          atomicOr(&p.status[0], kStatusBadOffsets);
+        }
+        if (nch[r] == 0) {
+          for (int q = 0; q < p.k; ++q) {
+            const long long o = static_cast<long long>(s) * p.k + q;
+            if (p.out_values32) p.out_values32[o] = p.pad_bits;
+            else p.out_values[o] = static_cast<uint16_t>(p.pad_bits);
+            p.out_indices[o] = -1;
+          }
         }
       }
+      csum += nch[r];
+      psum += (nch[r] + p.part_chunks - 1) / p.part_chunks;
     }
-    uint32_t tot;
-    const uint32_t pre = block_excl_scan<1024>(nch, &tot, warp_tot);
-    if (s < p.seg_num) p.chunk_start[s] = carry + pre;
+    uint32_t tot, ptot;
+    uint32_t run = carry + block_excl_scan<1024>(csum, &tot, warp_tot);
+    uint32_t prun = pcarry + block_excl_scan<1024>(psum, &ptot, warp_tot);
+#pragma unroll
+    for (int r = 0; r < kPrepPer; ++r) {
+      const int s = base + tid * kPrepPer + r;
+      if (s < p.seg_num) {
+        p.chunk_start[s] = run;
+        p.part_start[s] = prun;
+      }
+      run += nch[r];
+      prun += (nch[r] + p.part_chunks - 1) / p.part_chunks;
+    }
     carry += tot;
-    const uint32_t npart = (nch + p.part_chunks - 1) / p.part_chunks;
-    uint32_t ptot;
-    const uint32_t ppre = block_excl_scan<1024>(npart, &ptot, warp_tot);
-    if (s < p.seg_num) p.part_start[s] = pcarry + ppre;
     pcarry += ptot;
   }
   if (tid == 0) {
