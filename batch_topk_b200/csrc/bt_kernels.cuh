@@ -351,9 +351,9 @@ __device__ void producer_loop(const TopkParams& p, uint8_t* stages, uint64_t* fu
     long long s = b0 < p.seg_num ? b0 : static_cast<long long>(p.seg_num);
     bool own = true;
     // CSR: the set-up kernel clears the part count when the offsets are invalid (or every
-    // segment is empty): then no segment is touched
-    if (p.offsets && p.part_start[p.seg_num] == 0u) ok = false;
-    while (ok) {
+    // segment is empty): then no segment is touched, and only the stop item goes out
+    const bool work = !(p.offsets && p.part_start[p.seg_num] == 0u);
+    while (ok && work) {
       if (s >= p.seg_num) {
         own = false;
         // k > 128: help only once this block's consumers are through every stage filled so

@@ -144,3 +144,29 @@ def test_bad_offsets_beyond_max_total_len():
     flags, v, i = _csr_call(torch, vals, [0, 4000, 8000], 50, 6000)
     assert flags & bt.STATUS_BAD_OFFSETS
     assert (i == -7).all() and (v == 0x1234).all(), "a flagged call must not write rows"
+
+
+@pytest.mark.gpu
+def test_bad_offsets_many_segments_flag_only():
+    """More segments than resident blocks (whole segments, helping on) with offsets spanning
+    more than max_total_len: only BT_STATUS_BAD_OFFSETS is reported (the streaming kernel
+    still ends at once, with no wait running out), and no row is written."""
+    import torch
+
+    rng = np.random.default_rng(10)
+    vals = rng.standard_normal(8000).astype(np.float16).view(np.uint16)
+    off = list(range(0, 8001, 20))  # 400 segments of 20 values
+    flags, v, i = _csr_call(torch, vals, off, 8, 6000)
+    assert flags == bt.STATUS_BAD_OFFSETS, f"status {flags:#x}"
+    assert (i == -7).all() and (v == 0x1234).all(), "a flagged call must not write rows"
+
+
+@pytest.mark.gpu
+def test_all_empty_many_segments():
+    """400 empty CSR segments: every row is padding (-inf, index -1) and the status is clean."""
+    import torch
+
+    vals = np.zeros(16, np.uint16)
+    flags, v, i = _csr_call(torch, vals, [0] * 401, 8, 16)
+    assert flags == 0, f"status {flags:#x}"
+    assert (i == -1).all() and (v == 0xFC00).all()
